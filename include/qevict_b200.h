@@ -1,0 +1,183 @@
+/*
+ * qevict_b200.h -- C ABI of the B200 (sm_100a) Sticky-KV hot path.
+ *
+ * Plain device pointers and sizes; no framework types.  Every entry point is
+ * stream-ordered, never synchronises the host, never allocates, and returns
+ * QV_OK (0) or a negative QV_E* code for invalid arguments.  Problems that can
+ * only be seen on the device (an index outside a table, a window that is not
+ * where the layout says it is) set bits in the layer's device error word,
+ * which qv_read_error() copies out on demand.
+ *
+ * Layout of one layer's state in HBM ("slot layout").  For sequence b, KV head h:
+ *
+ *   main zone  K,V  [B][H][S_cap][D]  (kv dtype), S_cap = sink + k_windows*omega + ring_windows*omega
+ *       [0, sink)                                   attention sinks
+ *       [sink + s*omega, +omega)      s < k_windows  sticky slot s, holding window sticky_wid[b][h][s]
+ *       [sink + (k_windows + r)*omega, +omega)      ring slot r = w % ring_windows holds local window w
+ *   Q zone     kq,vq [B][H][q_windows][omega][D or D/2] u8, ks,kz [B][H][q_windows][D],
+ *              vs,vz [B][H][q_windows][omega]  (kv dtype); slot j holds window q_wid[b][h][j]
+ *
+ * Sticky and Q slots are unordered; sticky_order / q_order give the slot of
+ * each logical rank (sticky: ascending window id, as the reference keeps
+ * window_scores; Q: the reference's top-k order).  Only windows that change
+ * tier move during an eviction cycle.
+ *
+ * The reference (shaswata965-coder/Qevict) is Python/PyTorch; the entry points
+ * below replace the torch-op groups cited beside each one.  A ctypes binding
+ * is in qevict_b200/_native.py.
+ */
+#ifndef QEVICT_B200_H
+#define QEVICT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qv_stream_t; /* a cudaStream_t */
+
+enum {
+    QV_OK = 0,
+    QV_EINVAL = -1,     /* bad dimension / null pointer / unsupported combination */
+    QV_ENOTALIGNED = -2,/* prompt or local zone not a whole number of windows */
+    QV_ESPACE = -3,     /* workspace too small */
+    QV_ECUDA = -4,      /* a CUDA launch failed (see qv_last_cuda_error) */
+};
+
+enum { QV_F32 = 0, QV_BF16 = 1, QV_F16 = 2 };
+
+/* device error word bits (qv_read_error) */
+enum {
+    QV_DERR_TABLE = 1 << 0,    /* window id outside [0, max_windows) */
+    QV_DERR_LAYOUT = 1 << 1,   /* a window was not found where the layout says it is */
+    QV_DERR_CAPACITY = 1 << 2, /* more movers than free slots */
+};
+
+typedef struct qv_dims {
+    int32_t batch;        /* sequences decoded in lockstep */
+    int32_t kv_heads;     /* H */
+    int32_t group;        /* query heads per KV head (G) */
+    int32_t head_dim;     /* D: 64 or 128 */
+    int32_t omega;        /* window length, multiple of 16, <= 128 */
+    int32_t sink;         /* attention-sink tokens */
+    int32_t local;        /* local-zone tokens, multiple of omega */
+    int32_t k_windows;    /* sticky capacity (windows) */
+    int32_t q_windows;    /* Q-cache capacity (windows), may be 0 */
+    int32_t max_windows;  /* window-id table size */
+    int32_t bits;         /* 8 or 4 */
+    int32_t dtype;        /* QV_F32 / QV_BF16 / QV_F16 */
+} qv_dims;
+
+typedef struct qv_layer {
+    void* k;                 /* [B][H][S_cap][D] */
+    void* v;
+    uint8_t* kq;             /* [B][H][q_windows][omega][qbytes] */
+    uint8_t* vq;
+    void* ks;                /* [B][H][q_windows][D] */
+    void* kz;
+    void* vs;                /* [B][H][q_windows][omega] */
+    void* vz;
+    int32_t* sticky_wid;     /* [B][H][k_windows]  -1 = empty */
+    float* sticky_score;     /* [B][H][k_windows] */
+    int32_t* sticky_order;   /* [B][H][k_windows]  rank (ascending id) -> slot */
+    int32_t* q_wid;          /* [B][H][q_windows]  -1 = empty */
+    float* q_score;          /* [B][H][q_windows] */
+    int32_t* q_order;        /* [B][H][q_windows]  rank (top-k order) -> slot */
+    float* votes;            /* [B][H][S_cap] running attention votes (fp32) */
+    float* local_hist;       /* [B][H][max_windows] */
+    uint8_t* arch_valid;     /* [B][H][max_windows] path-C archive flags */
+    void* arch_ks;           /* [B][H][max_windows][D] */
+    void* arch_kz;
+    void* arch_vs;           /* [B][H][max_windows][omega] */
+    void* arch_vz;
+    int32_t* seq;            /* [B][4]: curr_k, q_count, reserved, reserved */
+    int32_t* step;           /* [4]: tokens in cache (incl. prompt), prompt length, reserved */
+    int32_t* err;            /* [1] device error word */
+} qv_layer;
+
+/* ---- sizes -------------------------------------------------------------- */
+int32_t qv_ring_windows(const qv_dims* d);            /* local/omega + 1 */
+int32_t qv_main_capacity(const qv_dims* d);           /* S_cap */
+size_t qv_decode_workspace_bytes(const qv_dims* d);
+size_t qv_cycle_workspace_bytes(const qv_dims* d);
+
+/* ---- decode step ------------------------------------------------------- */
+
+/* RoPE on the new query/key (HF rotate_half form) and in-place append of the
+ * new K/V token at its ring slot.  Replaces apply_rotary_pos_emb_single
+ * (src/models/kv_cache/helpers.py:56-62) applied at module.py:188-189 and the
+ * O(S) torch.cat append (src/models/attention/module.py:198-200).
+ * q_in [B][G*H][D], k_in/v_in [B][H][D]; cos/sin [max_pos][D] (kv dtype);
+ * q_out [B][G*H][D].  cos/sin may be NULL when the inputs are already rotated. */
+int qv_rope_append(const qv_dims* d, const qv_layer* L, const void* q_in, const void* k_in,
+                   const void* v_in, const void* cos_tab, const void* sin_tab, void* q_out,
+                   qv_stream_t stream);
+
+/* Fused split-K decode attention over [sinks | sticky slots | ring] plus the
+ * INT8/INT4 Q-cache, with the ledger fold.  Replaces compute_main_logits +
+ * compute_qcache_joint_softmax / compute_standard_softmax
+ * (src/models/attention/ops.py:23-46, 74-169, 176-212), the vote tally
+ * EvictionManager.tally_decode_scores (src/models/kv_cache/eviction_manager.py:198-203)
+ * and QuantizationManager.accumulate_scores (src/models/kv_cache/quantize_manager.py:101-111).
+ * q [B][G*H][D] rotated; out [B][G*H][D].  Advances step[0] by one token. */
+int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
+                        void* workspace, size_t workspace_bytes, qv_stream_t stream);
+
+/* One eviction cycle (every omega tokens): scoreboard, window competition,
+ * segmented top-k, promotion, Q-cache rebuild (paths A/B/C) and slot moves.
+ * Replaces EvictionManager.run_decode_cycle / update_local_history /
+ * commit_decode_result / reset_decode_counters (eviction_manager.py:205-417),
+ * QuantizationManager.get_promoted_windows / rebuild (quantize_manager.py:114-327)
+ * and STICKYKVCache_LayerWise._build_physical_cache (src/models/kv_cache/cache.py:433-575). */
+int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                   qv_stream_t stream);
+
+/* ---- prefill ----------------------------------------------------------- */
+
+/* Build the layer state from a prompt: window tally, top-k/top-q selection,
+ * Q-cache store, compaction into the slot layout.  Replaces the prefill branch
+ * of STICKYKVCache_LayerWise.__call__ (cache.py:269-355): tally_prefill_scores
+ * (eviction_manager.py:115-173), evict_from_window_scores (eviction.py:102-156),
+ * store_windows (quantize_manager.py:91-98),
+ * create_mask_and_evict_from_kv_cache_prompt_stage (eviction.py:163-240).
+ * k_prompt/v_prompt [B][H][S][D] rotated; colsum [B][H][S] per-key column sums
+ * (score_dtype QV_F32 for the flash path, or the kv dtype for the SDPA path,
+ * whose window sums the reference rounds to that dtype). */
+int qv_prefill_build(const qv_dims* d, const qv_layer* L, const void* k_prompt, const void* v_prompt,
+                     int32_t prompt_len, const void* colsum, int32_t score_dtype, qv_stream_t stream);
+
+/* Causal prefill attention that also emits the per-key column sums of the
+ * GQA-group-mean softmax (512-query chunks rounded to the kv dtype, fp32
+ * across chunks).  Replaces flash_attn_func + compute_chunked_prefill_scores
+ * (src/models/attention/ops_flash.py:22-141).
+ * q [B][S][G*H][D], k,v [B][S][H][D] (rotated); out [B][S][G*H][D]; colsum [B][H][S] fp32. */
+int qv_prefill_attention(const qv_dims* d, const void* q, const void* k, const void* v, int32_t seq_len,
+                         void* out, float* colsum, void* workspace, size_t workspace_bytes,
+                         qv_stream_t stream);
+size_t qv_prefill_workspace_bytes(const qv_dims* d, int32_t seq_len);
+
+/* ---- codec (the reference's static methods) ----------------------------- */
+
+/* quantize_k_per_window / quantize_v_per_window / dequantize_from_quant
+ * (src/models/kv_cache/quantize.py:19-71), for n windows of [omega][D]:
+ * x [n][omega][D]; codes [n][omega][D or D/2]; K: scale/zp [n][D]; V: scale/zp [n][omega]. */
+int qv_quantize_k(int32_t n, int32_t omega, int32_t head_dim, int32_t bits, int32_t dtype,
+                  const void* x, uint8_t* codes, void* scale, void* zp, qv_stream_t stream);
+int qv_quantize_v(int32_t n, int32_t omega, int32_t head_dim, int32_t bits, int32_t dtype,
+                  const void* x, uint8_t* codes, void* scale, void* zp, qv_stream_t stream);
+/* per_token = 0: scale/zp [n][D] (K); 1: scale/zp [n][omega] (V) */
+int qv_dequantize(int32_t n, int32_t omega, int32_t head_dim, int32_t bits, int32_t dtype,
+                  int32_t per_token, const uint8_t* codes, const void* scale, const void* zp,
+                  void* out, qv_stream_t stream);
+
+/* ---- diagnostics ------------------------------------------------------- */
+int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* synchronises the stream */
+const char* qv_last_cuda_error(void);
+const char* qv_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QEVICT_B200_H */

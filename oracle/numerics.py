@@ -61,17 +61,21 @@ def mean_round(x, axis, dt):
 
 
 def tree_sum32(x):
-    """Sum the last axis (length 64) in the order a 32-lane warp reduces it.
+    """Sum the last axis (one window's omega values, omega <= 128) in warp order.
 
-    Lane i first adds elements i and i+32, then the lanes combine with an
-    xor-butterfly over offsets 16, 8, 4, 2, 1 -- all in fp32.  The CUDA
-    scoreboard kernel sums each window's 64 votes in exactly this order, so the
-    oracle uses it too when it must agree with the kernel bit-for-bit.
+    Lane l (0..31) accumulates x[l], x[l+32], x[l+64], ... sequentially in fp32;
+    the 32 lanes then combine by xor-butterfly over offsets 16, 8, 4, 2, 1.
+    The CUDA scoreboard kernel sums each window's votes in exactly this order,
+    so the oracle uses it too when it must agree with the kernel bit-for-bit.
     """
     x = f32(x)
     n = x.shape[-1]
-    assert n == 64, "tree order is defined for 64-token windows"
-    a = (x[..., :32] + x[..., 32:]).astype(np.float32)
+    a = np.zeros(x.shape[:-1] + (32,), np.float32)
+    for lane in range(min(32, n)):
+        acc = x[..., lane]
+        for i in range(lane + 32, n, 32):
+            acc = (acc + x[..., i]).astype(np.float32)
+        a[..., lane] = acc
     off = 16
     idx = np.arange(32)
     while off >= 1:

@@ -137,9 +137,10 @@ class OracleStickyLayer:
         nw = (score_end - sink) // om
         score_end = sink + nw * om
         self.dyn_local = self.local_num
+        wsum = self._prefill_window_sums
         if nw > 0:
             obs = sum_round(attn[:, :seq_len, sink:score_end], 1, attn_dt)
-            win = f32(sum_round(obs.reshape(H, nw, om), 2, attn_dt))
+            win = wsum(obs.reshape(H, nw, om), attn_dt)
             idx = np.arange(nw, dtype=np.float32)
             self.window_scores[:, :nw, 0] = win
             self.window_scores[:, :nw, 1] = idx
@@ -151,8 +152,14 @@ class OracleStickyLayer:
             afr = sink + tpw * om
             if tpw > 0:
                 full = sum_round(attn[:, :seq_len, sink:afr], 1, attn_dt)
-                self.local_history[:, :tpw] = f32(sum_round(full.reshape(H, tpw, om), 2, attn_dt))
+                self.local_history[:, :tpw] = wsum(full.reshape(H, tpw, om), attn_dt)
         return score_end
+
+    def _prefill_window_sums(self, x, attn_dt):
+        """``.view(H, nw, omega).sum(dim=2)`` in the scores' dtype (eviction_manager.py:141-143)."""
+        if self.window_sum == "tree":
+            return rnd(tree_sum32(x), attn_dt)
+        return f32(sum_round(x, 2, attn_dt))
 
     def evict_from_window_scores(self):
         """eviction.py:102-156 (mutates window_scores, returns top-q losers)."""
@@ -257,7 +264,7 @@ class OracleStickyLayer:
                     buckets.setdefault(int(w), []).append(n_new_votes[h, j])
             for w, vals in buckets.items():
                 vals = f32(vals)
-                if vals.size == 64:
+                if vals.size == self.omega:
                     sb[h, w] = tree_sum32(vals)
                 else:
                     acc = np.float32(0)
@@ -512,10 +519,18 @@ class OracleStickyLayer:
         q_scores [H, W*omega] or None
         Returns (K', V') -- the same arrays, or the rebuilt cache on cycle steps.
         """
+        if not self.tally(K, scores, q_scores, score_dt):
+            return K, V
+        return self.cycle(K, V)
+
+    def tally(self, K, scores, q_scores, score_dt):
+        """Counters + ledger accumulation of one decode token (cache.py:357-376,
+        eviction_manager.py:198-203, quantize_manager.py:101-111).
+        Returns True when an eviction cycle is due."""
         self.global_counter += 1
         S = K.shape[1]
         if self.lid is None:
-            return K, V
+            return False
         self.n_tokens += 1
         self.gen_step += 1
         self.votes[:, :S] = (self.votes[:, :S] + f32(scores)[:, :S]).astype(np.float32)
@@ -526,8 +541,11 @@ class OracleStickyLayer:
             if q_scores.shape[1] >= tot:
                 per_w = sum_round(f32(q_scores)[:, :tot].reshape(self.H, qc, self.omega), 2, score_dt)
                 self.q["scores"] = (self.q["scores"] + f32(per_w)).astype(np.float32)
-        if self.tokens_since != self.omega:
-            return K, V
+        return self.tokens_since == self.omega
+
+    def cycle(self, K, V):
+        """The eviction cycle of cache.py:378-427 on the current ledger."""
+        S = K.shape[1]
         res = self.run_decode_cycle(S)
         self.last_result = res
         self.update_local_history(res)

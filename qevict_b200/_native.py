@@ -1,0 +1,98 @@
+"""ctypes binding of the C ABI declared in include/qevict_b200.h.
+
+The shared library is built in-tree (``qevict_b200/_lib/libqevict_b200.so``)
+by ``qevict_b200.build.build()``.  There is no fallback: importing a compute
+entry point without the library raises immediately.
+"""
+
+import ctypes
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libqevict_b200.so")
+
+QV_OK, QV_EINVAL, QV_ENOTALIGNED, QV_ESPACE, QV_ECUDA = 0, -1, -2, -3, -4
+QV_F32, QV_BF16, QV_F16 = 0, 1, 2
+QV_DERR_TABLE, QV_DERR_LAYOUT, QV_DERR_CAPACITY = 1, 2, 4
+
+_ERRNAMES = {QV_EINVAL: "invalid argument", QV_ENOTALIGNED: "prompt/local zone not window-aligned",
+             QV_ESPACE: "workspace too small", QV_ECUDA: "CUDA error"}
+
+
+class QvDims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "batch", "kv_heads", "group", "head_dim", "omega", "sink", "local", "k_windows",
+        "q_windows", "max_windows", "bits", "dtype")]
+
+
+class QvLayer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "k", "v", "kq", "vq", "ks", "kz", "vs", "vz", "sticky_wid", "sticky_score",
+        "sticky_order", "q_wid", "q_score", "q_order", "votes", "local_hist", "arch_valid",
+        "arch_ks", "arch_kz", "arch_vs", "arch_vz", "seq", "step", "err")]
+
+
+class QevictError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    """Load the native library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH):
+        raise QevictError(
+            f"qevict_b200 native library not found at {_LIB_PATH}; build it with "
+            "`python -c 'import qevict_b200.build as b; b.build()'` (nvcc, sm_100a)")
+    L = ctypes.CDLL(_LIB_PATH)
+    P = ctypes.POINTER
+    vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+    D, Lp = P(QvDims), P(QvLayer)
+    sig = {
+        "qv_ring_windows": (i32, [D]),
+        "qv_main_capacity": (i32, [D]),
+        "qv_decode_workspace_bytes": (sz, [D]),
+        "qv_cycle_workspace_bytes": (sz, [D]),
+        "qv_rope_append": (ctypes.c_int, [D, Lp, vp, vp, vp, vp, vp, vp, vp]),
+        "qv_decode_attention": (ctypes.c_int, [D, Lp, vp, vp, vp, sz, vp]),
+        "qv_evict_cycle": (ctypes.c_int, [D, Lp, vp, sz, vp]),
+        "qv_prefill_build": (ctypes.c_int, [D, Lp, vp, vp, i32, vp, i32, vp]),
+        "qv_prefill_attention": (ctypes.c_int, [D, vp, vp, vp, i32, vp, vp, vp, sz, vp]),
+        "qv_prefill_workspace_bytes": (sz, [D, i32]),
+        "qv_quantize_k": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
+        "qv_quantize_v": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
+        "qv_dequantize": (ctypes.c_int, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
+        "qv_read_error": (ctypes.c_int, [Lp, P(i32), vp]),
+        "qv_last_cuda_error": (ctypes.c_char_p, []),
+        "qv_version": (ctypes.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def exported_symbols():
+    """Names the header declares (used by the CPU test that checks the exports)."""
+    return ["qv_ring_windows", "qv_main_capacity", "qv_decode_workspace_bytes",
+            "qv_cycle_workspace_bytes", "qv_rope_append", "qv_decode_attention", "qv_evict_cycle",
+            "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
+            "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_read_error",
+            "qv_last_cuda_error", "qv_version"]
+
+
+def check(rc, what):
+    if rc != QV_OK:
+        msg = _ERRNAMES.get(rc, f"error {rc}")
+        if rc == QV_ECUDA:
+            msg += ": " + lib().qv_last_cuda_error().decode()
+        raise QevictError(f"{what} failed: {msg}")
+
+
+def ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
