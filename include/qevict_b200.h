@@ -115,6 +115,14 @@ int qv_rope_append(const qv_dims* d, const qv_layer* L, const void* q_in, const 
                    const void* v_in, const void* cos_tab, const void* sin_tab, void* q_out,
                    qv_stream_t stream);
 
+/* RoPE of a token-major block x[batch][seq][heads][head_dim] at positions
+ * pos0 .. pos0+seq-1, in place, HF rotate_half form with the reference's
+ * rounding: (x*cos) + (rotate_half(x)*sin), each op rounded to the dtype
+ * (src/models/kv_cache/helpers.py:56-62, applied at module.py:188-189 for the
+ * prompt).  cos/sin [max_pos][head_dim] in the same dtype. */
+int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t dtype, void* x,
+            const void* cos_tab, const void* sin_tab, int32_t pos0, qv_stream_t stream);
+
 /* Fused split-K decode attention over [sinks | sticky slots | ring] plus the
  * INT8/INT4 Q-cache, with the ledger fold.  Replaces compute_main_logits +
  * compute_qcache_joint_softmax / compute_standard_softmax

@@ -71,6 +71,17 @@ inline Geo make_geo(const qv_dims* d) {
 }
 
 int validate_dims(const qv_dims* d);
+
+// Raise a kernel's dynamic shared-memory limit only when a launch needs more
+// than any earlier one did, so that steady-state launches (and CUDA-graph
+// captures) make no attribute calls.
+template <typename K>
+inline cudaError_t ensure_smem(K kernel, size_t bytes, int* cached) {
+    if ((int)bytes <= *cached) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) *cached = (int)bytes;
+    return e;
+}
 int set_cuda_error(cudaError_t e);
 int check_launch();
 

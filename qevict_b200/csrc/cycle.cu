@@ -434,7 +434,8 @@ extern "C" int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspa
     const size_t per_warp = (select_smem_per_warp(g) + 15) & ~(size_t)15;
     const size_t smem = per_warp * g.H;
     if (smem > 220 * 1024) return QV_EINVAL;
-    cudaError_t e = cudaFuncSetAttribute(cycle_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static int cached = 48 * 1024;
+    cudaError_t e = ensure_smem(cycle_select_kernel, smem, &cached);
     if (e != cudaSuccess) return set_cuda_error(e);
     cudaStream_t s = (cudaStream_t)stream;
     cycle_select_kernel<<<g.B, 32 * g.H, smem, s>>>(g, *L, w, (int)per_warp);

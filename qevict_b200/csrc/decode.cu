@@ -317,9 +317,44 @@ __global__ void rope_append_kernel(Geo g, qv_layer L, const void* __restrict__ q
     }
 }
 
+// RoPE of a token-major block x[b][s][head][d] at positions pos0 + s (in place).
+template <int DT>
+__global__ void rope_tokens_kernel(int heads, int D, void* __restrict__ x, const void* __restrict__ cos_t,
+                                   const void* __restrict__ sin_t, int S, int pos0) {
+    const size_t row = blockIdx.x;  // (b * S + s) * heads + head
+    const int s = (int)((row / heads) % S);
+    const int pos = pos0 + s;
+    const int half = D / 2;
+    extern __shared__ float rrow[];
+    for (int d = threadIdx.x; d < D; d += blockDim.x) rrow[d] = ld<DT>(x, row * D + d);
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float xv = rrow[d];
+        const float xr = d < half ? -rrow[d + half] : rrow[d - half];
+        const float c = ld<DT>(cos_t, (size_t)pos * D + d), sn = ld<DT>(sin_t, (size_t)pos * D + d);
+        st<DT>(x, row * D + d, add_r<DT>(mul_r<DT>(xv, c), mul_r<DT>(xr, sn)));
+    }
+}
+
 }  // namespace qv
 
 using namespace qv;
+
+extern "C" int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t dtype, void* x,
+                       const void* cos_tab, const void* sin_tab, int32_t pos0, qv_stream_t stream) {
+    if (batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2 || !x || !cos_tab || !sin_tab || pos0 < 0)
+        return QV_EINVAL;
+    const size_t rows = (size_t)batch * seq * heads;
+    const size_t sm = head_dim * sizeof(float);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (dtype) {
+        case QV_F32: rope_tokens_kernel<QV_F32><<<rows, 128, sm, s>>>(heads, head_dim, x, cos_tab, sin_tab, seq, pos0); break;
+        case QV_BF16: rope_tokens_kernel<QV_BF16><<<rows, 128, sm, s>>>(heads, head_dim, x, cos_tab, sin_tab, seq, pos0); break;
+        case QV_F16: rope_tokens_kernel<QV_F16><<<rows, 128, sm, s>>>(heads, head_dim, x, cos_tab, sin_tab, seq, pos0); break;
+        default: return QV_EINVAL;
+    }
+    return check_launch();
+}
 
 extern "C" size_t qv_decode_workspace_bytes(const qv_dims* d) {
     if (validate_dims(d)) return 0;

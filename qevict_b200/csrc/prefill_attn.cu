@@ -245,9 +245,10 @@ template <int DT, int D>
 static int launch_prefill(const Geo& g, const void* q, const void* k, const void* v, int S, void* out,
                           float* colsum, float* stats, cudaStream_t s) {
     const size_t fs = fwd_smem(D), cs = col_smem(D);
-    cudaError_t e = cudaFuncSetAttribute(prefill_fwd_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs);
+    static int c1 = 48 * 1024, c2 = 48 * 1024;
+    cudaError_t e = ensure_smem(prefill_fwd_kernel<DT, D>, fs, &c1);
     if (e != cudaSuccess) return set_cuda_error(e);
-    e = cudaFuncSetAttribute(prefill_colsum_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cs);
+    e = ensure_smem(prefill_colsum_kernel<DT, D>, cs, &c2);
     if (e != cudaSuccess) return set_cuda_error(e);
     dim3 g1((S + PT - 1) / PT, g.H * g.G, g.B);
     prefill_fwd_kernel<DT, D><<<g1, PA_THREADS, fs, s>>>(g, q, k, v, S, out, stats);

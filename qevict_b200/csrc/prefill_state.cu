@@ -166,8 +166,8 @@ extern "C" int qv_prefill_build(const qv_dims* d, const qv_layer* L, const void*
     const int BH = g.B * g.H;
 #define QV_PF_SEL(SD)                                                                                  \
     do {                                                                                               \
-        cudaError_t e = cudaFuncSetAttribute(prefill_select_kernel<SD>,                                \
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);  \
+        static int cached = 48 * 1024;                                                                 \
+        cudaError_t e = ensure_smem(prefill_select_kernel<SD>, smem, &cached);                         \
         if (e != cudaSuccess) return set_cuda_error(e);                                                \
         prefill_select_kernel<SD><<<BH, PF_THREADS, smem, s>>>(g, *L, colsum, S);                      \
     } while (0)
