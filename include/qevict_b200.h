@@ -68,7 +68,18 @@ typedef struct qv_dims {
     int32_t max_windows;  /* window-id table size */
     int32_t bits;         /* 8 or 4 */
     int32_t dtype;        /* QV_F32 / QV_BF16 / QV_F16 */
+    int32_t flags;        /* QV_FLAG_* */
 } qv_dims;
+
+/* qv_dims.flags */
+enum {
+    /* Decode attention dequantises Q-cache codes with the reference's own
+     * rounding, rnd(rnd(code*scale) + zp) in the KV dtype (quantize.py:62-71),
+     * on the CUDA-core kernel.  Without the flag, head_dim-128 / omega-64 /
+     * INT8 / BF16-or-FP16 layers use the tensor-core kernel, which applies the
+     * scale and zero point exactly in fp32 instead. */
+    QV_FLAG_REFERENCE_ROUNDING = 1,
+};
 
 typedef struct qv_layer {
     void* k;                 /* [B][H][S_cap][D] */
@@ -101,6 +112,15 @@ typedef struct qv_layer {
 int32_t qv_ring_windows(const qv_dims* d);            /* local/omega + 1 */
 int32_t qv_main_capacity(const qv_dims* d);           /* S_cap */
 size_t qv_decode_workspace_bytes(const qv_dims* d);
+/* Which decode-attention kernel qv_decode_attention runs for these dims:
+ * 0 = CUDA-core kernel with the reference's dequantisation rounding,
+ * 1 = tensor-core kernel (TMA pipeline, exact fp32 dequantisation). */
+int32_t qv_decode_path(const qv_dims* d);
+/* Byte offset, inside the decode workspace, of the rounded logits the last
+ * qv_decode_attention wrote: [B*H][S_cap + q_windows*omega][group] in the KV
+ * dtype, main-zone positions in slot layout followed by the Q slots (used by
+ * the parity tests to separate accumulation-order effects from the rest). */
+size_t qv_decode_logits_offset(const qv_dims* d);
 size_t qv_cycle_workspace_bytes(const qv_dims* d);
 
 /* ---- decode step ------------------------------------------------------- */

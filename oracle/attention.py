@@ -23,37 +23,88 @@ from .codec import dequantize_from_quant
 from .numerics import f32, op, rnd, mean_round
 
 
-def _logits(q, k, dt):
+def _exact_dequant(codes, scale, zp, bit_width):
+    codes = np.asarray(codes)
+    if bit_width == 4:
+        hi = (codes >> 4) & 0x0F
+        lo = codes & 0x0F
+        codes = np.stack([hi, lo], axis=-1).reshape(*codes.shape[:-1], -1)
+    return codes.astype(np.float64) * np.asarray(scale, np.float64) + np.asarray(zp, np.float64)
+
+
+def _ulp(x, dt):
+    """One unit in the last place of dtype dt at |x| (float64 array)."""
+    bits = {"fp32": 23, "bf16": 7, "fp16": 10}[dt]
+    ax = np.maximum(np.abs(np.asarray(x, np.float64)), 1e-30)
+    return 2.0 ** (np.floor(np.log2(ax)) - bits)
+
+
+def _logits(q, k, dt, raw=False):
     """q [H, G, D], k [H, S, D] -> logits [H, G, S] in dt (ops.py:35-41)."""
-    raw = np.einsum("hgd,hsd->hgs", q.astype(np.float64), k.astype(np.float64))
-    raw = rnd(raw, dt)
-    return op(np.divide, dt, raw, np.float32(math.sqrt(q.shape[-1])))
+    r = np.einsum("hgd,hsd->hgs", q.astype(np.float64), k.astype(np.float64))
+    lg = op(np.divide, dt, rnd(r, dt), np.float32(math.sqrt(q.shape[-1])))
+    return (lg, r) if raw else lg
 
 
-def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8):
+def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="reference",
+                     logits_override=None, return_extras=False):
     """Attention of one decode token.
+
+    dequant="reference" dequantises the Q-cache the way the reference does,
+    rnd(rnd(code * scale) + zp) in the KV dtype (quantize.py:62-71);
+    dequant="exact" applies scale and zero point without intermediate
+    rounding (code * scale + zp in float64), which is what the tensor-core
+    kernel computes.  The two differ by the reference's rounding of the
+    intermediate code*scale (up to half an ulp of the KV dtype at |code*scale|,
+    e.g. 2^-6 for values in [4, 8) in bf16).
 
     q        [Hq, D]  rotated query (values in dt)
     k_main   [H, S, D], v_main [H, S, D] physical main cache incl. the new token
     qcache   None or dict(kq [H,W,w,D] u8, ks [H,W,1,D], kz [H,W,1,D],
                           vq [H,W,w,D] u8, vs [H,W,w,1], vz [H,W,w,1])
+    logits_override: [H, G, S + W*w] rounded logits to use instead of the
+        ones computed here (lets a test feed the kernel's own logits through the
+        rest of the computation).
     Returns (out [Hq, D] in dt, scores_main [H, S] in dt, scores_q [H, W*w] in dt or None)
+    and, with return_extras, a dict with the logits, the raw (pre-rounding) dot
+    products and the bound on |kernel logit - oracle logit| per token.
     """
     q = f32(q)
     H, S, D = k_main.shape
     G = q.shape[0] // H
     qg = q.reshape(H, G, D)
-    main = _logits(qg, f32(k_main), dt)  # [H, G, S]
+    main, raw_main = _logits(qg, f32(k_main), dt, raw=True)  # [H, G, S]
+    absdot = np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)), np.abs(f32(k_main).astype(np.float64)))
+    fold = None
     if qcache is not None:
-        kdq = dequantize_from_quant(qcache["kq"], qcache["ks"], qcache["kz"], dt, bit_width)
-        vdq = dequantize_from_quant(qcache["vq"], qcache["vs"], qcache["vz"], dt, bit_width)
+        if dequant == "exact":
+            kdq = _exact_dequant(qcache["kq"], qcache["ks"], qcache["kz"], bit_width)
+            vdq = _exact_dequant(qcache["vq"], qcache["vs"], qcache["vz"], bit_width)
+        else:
+            kdq = dequantize_from_quant(qcache["kq"], qcache["ks"], qcache["kz"], dt, bit_width)
+            vdq = dequantize_from_quant(qcache["vq"], qcache["vs"], qcache["vz"], dt, bit_width)
         Hc, W, w, _ = kdq.shape
         kdq = kdq.reshape(H, W * w, D)
         vdq = vdq.reshape(H, W * w, D)
-        ql = _logits(qg, kdq, dt)
+        ql, raw_q = _logits(qg, kdq, dt, raw=True)
         all_l = np.concatenate([main, ql], axis=-1)
+        raw = np.concatenate([raw_main, raw_q], axis=-1)
+        absdot = np.concatenate([absdot, np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)), np.abs(kdq))], axis=-1)
+        if dequant == "exact":
+            # the kernel folds the K scale into q and rounds q*scale to fp16
+            codes = np.asarray(qcache["kq"])
+            if bit_width == 4:
+                codes = np.stack([(codes >> 4) & 15, codes & 15], -1).reshape(*codes.shape[:-1], -1)
+            qs = np.abs(qg[:, :, None, None, :].astype(np.float64) * np.asarray(qcache["ks"], np.float64)[:, None])
+            fold = np.einsum("hgwkd,hwtd->hgwt", qs, codes.astype(np.float64)) * 2.0 ** -11
+            # fp32 accumulation of the 1024-offset products inside the MMA
+            fold = fold + (np.sum(qs, axis=(3, 4))[..., None] * 1024.0 * 2.0 ** -20)
+            fold = fold.reshape(H, G, -1)
     else:
         all_l = main
+        raw = raw_main
+    if logits_override is not None:
+        all_l = f32(logits_override)
     x = all_l.astype(np.float64)
     m = x.max(axis=-1, keepdims=True)
     e = np.exp(x - m)
@@ -62,10 +113,26 @@ def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8):
     pm = p[..., :S]
     out = rnd(np.einsum("hgs,hsd->hgd", pm.astype(np.float64), f32(v_main).astype(np.float64)), dt)
     scores_q = None
+    out_main, out_q = out, None
     if qcache is not None:
         pq = p[..., S:]
         out_q = rnd(np.einsum("hgs,hsd->hgd", pq.astype(np.float64), vdq.astype(np.float64)), dt)
         out = op(np.add, dt, out, out_q)
         scores_q = mean_round(pq, 1, dt)
     scores_main = mean_round(pm, 1, dt)
-    return out.reshape(H * G, D), scores_main, scores_q
+    if not return_extras:
+        return out.reshape(H * G, D), scores_main, scores_q
+    # one ulp of the dtype at the rounded dot product, divided by sqrt(D), plus one
+    # ulp at the logit, plus the fp16 scale-folding error of Q-cache tokens
+    sd = math.sqrt(D)
+    # fp32 accumulation of the D products (any order): at most ~64 u * sum|q_d k_d|
+    acc = absdot * 64.0 * 2.0 ** -24
+    bound = (_ulp(raw, dt) / sd + _ulp(all_l, dt) + acc / sd) * 1.01
+    if fold is not None:
+        bound[..., S:] += fold / sd
+    # the reference rounds out_main and out_q separately (ops.py:150): an
+    # implementation whose pre-rounding values differ by a hair can land one
+    # ulp away on either, so outputs are compared with these two ulps added
+    out_ulps = _ulp(out_main, dt) + (_ulp(out_q, dt) if out_q is not None else 0.0)
+    return out.reshape(H * G, D), scores_main, scores_q, dict(
+        logits=all_l, raw=raw, bound=bound, out_ulps=out_ulps.reshape(H * G, D))

@@ -21,7 +21,9 @@ _ERRNAMES = {QV_EINVAL: "invalid argument", QV_ENOTALIGNED: "prompt/local zone n
 class QvDims(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in (
         "batch", "kv_heads", "group", "head_dim", "omega", "sink", "local", "k_windows",
-        "q_windows", "max_windows", "bits", "dtype")]
+        "q_windows", "max_windows", "bits", "dtype", "flags")]
+
+QV_FLAG_REFERENCE_ROUNDING = 1
 
 
 class QvLayer(ctypes.Structure):
@@ -55,6 +57,8 @@ def lib():
         "qv_ring_windows": (i32, [D]),
         "qv_main_capacity": (i32, [D]),
         "qv_decode_workspace_bytes": (sz, [D]),
+        "qv_decode_path": (i32, [D]),
+        "qv_decode_logits_offset": (sz, [D]),
         "qv_cycle_workspace_bytes": (sz, [D]),
         "qv_rope_append": (ctypes.c_int, [D, Lp, vp, vp, vp, vp, vp, vp, vp]),
         "qv_decode_attention": (ctypes.c_int, [D, Lp, vp, vp, vp, sz, vp]),
@@ -80,7 +84,8 @@ def lib():
 
 def exported_symbols():
     """Names the header declares (used by the CPU test that checks the exports)."""
-    return ["qv_ring_windows", "qv_main_capacity", "qv_decode_workspace_bytes",
+    return ["qv_ring_windows", "qv_main_capacity", "qv_decode_workspace_bytes", "qv_decode_path",
+            "qv_decode_logits_offset",
             "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention", "qv_evict_cycle",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_read_error",

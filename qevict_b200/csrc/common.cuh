@@ -51,7 +51,7 @@ template <int DT> __device__ __forceinline__ void st(void* p, size_t i, float x)
 // Geometry of one layer, computed once on the host.
 // ---------------------------------------------------------------------------
 struct Geo {
-    int B, H, G, D, om, sink, local, kw, qw, maxW, bits, dt;
+    int B, H, G, D, om, sink, local, kw, qw, maxW, bits, dt, flags;
     int R;       // ring windows = local/om + 1
     int S_cap;   // sink + (kw + R) * om
     int qbytes;  // bytes of one code row: D (INT8) or D/2 (INT4)
@@ -63,7 +63,7 @@ inline Geo make_geo(const qv_dims* d) {
     Geo g;
     g.B = d->batch; g.H = d->kv_heads; g.G = d->group; g.D = d->head_dim; g.om = d->omega;
     g.sink = d->sink; g.local = d->local; g.kw = d->k_windows; g.qw = d->q_windows;
-    g.maxW = d->max_windows; g.bits = d->bits; g.dt = d->dtype;
+    g.maxW = d->max_windows; g.bits = d->bits; g.dt = d->dtype; g.flags = d->flags;
     g.R = (d->omega > 0) ? d->local / d->omega + 1 : 0;
     g.S_cap = g.sink + (g.kw + g.R) * g.om;
     g.qbytes = g.bits == 4 ? g.D / 2 : g.D;

@@ -15,6 +15,7 @@
 // writes the output and folds the exact probabilities into the ledger.  The
 // last of all merges advances the token counter.
 #include <math.h>
+#include <stdlib.h>
 
 #include "codec.cuh"
 
@@ -280,40 +281,39 @@ decode_split_kernel(Geo g, qv_layer L, const void* __restrict__ q, DecodeWs ws, 
 }
 
 // ---- RoPE + append ----------------------------------------------------------
+// One CTA per (sequence, row): rows are the G*H query heads, then the H new keys,
+// then the H new values.  blockDim = D.
 template <int DT>
 __global__ void rope_append_kernel(Geo g, qv_layer L, const void* __restrict__ q_in, const void* __restrict__ k_in,
                                    const void* __restrict__ v_in, const void* __restrict__ cos_t,
                                    const void* __restrict__ sin_t, void* __restrict__ q_out) {
-    const int b = blockIdx.x;
+    // the attention kernel may start its prologue now (it waits for this grid)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int b = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
     const int N0 = L.step[0];
-    const int w = (N0 - g.sink) / g.om;
-    const int off = (N0 - g.sink) % g.om;
-    const int ppos = g.ring_base() + (w % g.R) * g.om + off;
     const int D = g.D, half = D / 2;
     const int nq = g.H * g.G;
-    const int rows = nq + 2 * g.H;
-    for (int idx = threadIdx.x; idx < rows * D; idx += blockDim.x) {
-        const int r = idx / D, d = idx % D;
-        const void* src;
-        size_t si;
-        if (r < nq) { src = q_in; si = ((size_t)b * nq + r) * D; }
-        else if (r < nq + g.H) { src = k_in; si = ((size_t)b * g.H + (r - nq)) * D; }
-        else { src = v_in; si = ((size_t)b * g.H + (r - nq - g.H)) * D; }
-        float x = ld<DT>(src, si + d);
-        const bool rot = cos_t != nullptr && r < nq + g.H;
-        if (rot) {
-            // (x * cos) + (rotate_half(x) * sin)   (helpers.py:56-62)
-            const float xr = d < half ? -ld<DT>(src, si + d + half) : ld<DT>(src, si + d - half);
-            const float c = ld<DT>(cos_t, (size_t)N0 * D + d), s = ld<DT>(sin_t, (size_t)N0 * D + d);
-            x = add_r<DT>(mul_r<DT>(x, c), mul_r<DT>(xr, s));
-        }
-        if (r < nq) {
-            st<DT>(q_out, si + d, x);
-        } else {
-            const int hh = r < nq + g.H ? r - nq : r - nq - g.H;
-            void* dst = r < nq + g.H ? L.k : L.v;
-            st<DT>(dst, (((size_t)b * g.H + hh) * g.S_cap + ppos) * D + d, x);
-        }
+    const void* src;
+    size_t si;
+    if (r < nq) { src = q_in; si = ((size_t)b * nq + r) * D; }
+    else if (r < nq + g.H) { src = k_in; si = ((size_t)b * g.H + (r - nq)) * D; }
+    else { src = v_in; si = ((size_t)b * g.H + (r - nq - g.H)) * D; }
+    float x = ld<DT>(src, si + d);
+    if (cos_t != nullptr && r < nq + g.H) {
+        // (x * cos) + (rotate_half(x) * sin)   (helpers.py:56-62)
+        const float xr = d < half ? -ld<DT>(src, si + d + half) : ld<DT>(src, si + d - half);
+        const float c = ld<DT>(cos_t, (size_t)N0 * D + d), sn = ld<DT>(sin_t, (size_t)N0 * D + d);
+        x = add_r<DT>(mul_r<DT>(x, c), mul_r<DT>(xr, sn));
+    }
+    if (r < nq) {
+        st<DT>(q_out, si + d, x);
+    } else {
+        const int w = (N0 - g.sink) / g.om;
+        const int off = (N0 - g.sink) % g.om;
+        const int ppos = g.ring_base() + (w % g.R) * g.om + off;
+        const int hh = r < nq + g.H ? r - nq : r - nq - g.H;
+        void* dst = r < nq + g.H ? L.k : L.v;
+        st<DT>(dst, (((size_t)b * g.H + hh) * g.S_cap + ppos) * D + d, x);
     }
 }
 
@@ -336,6 +336,11 @@ __global__ void rope_tokens_kernel(int heads, int D, void* __restrict__ x, const
     }
 }
 
+// tensor-core kernel for the production shape (decode_mma.cu)
+bool mm_supported(const Geo& g);
+size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits);
+int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s);
+
 }  // namespace qv
 
 using namespace qv;
@@ -356,12 +361,34 @@ extern "C" int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_d
     return check_launch();
 }
 
+extern "C" int32_t qv_decode_path(const qv_dims* d) {
+    if (validate_dims(d)) return -1;
+    return mm_supported(make_geo(d)) ? 1 : 0;
+}
+
+extern "C" size_t qv_decode_logits_offset(const qv_dims* d) {
+    if (validate_dims(d)) return 0;
+    Geo g = make_geo(d);
+    size_t a, b, t;
+    if (mm_supported(g)) {
+        mm_ws_bytes(g, &a, &b);
+        return b;
+    }
+    int nm, nq;
+    decode_ws_layout(g, &a, &b, &t, &nm, &nq);
+    return b;
+}
+
 extern "C" size_t qv_decode_workspace_bytes(const qv_dims* d) {
     if (validate_dims(d)) return 0;
     Geo g = make_geo(d);
     size_t a, b, t;
     int nm, nq;
     decode_ws_layout(g, &a, &b, &t, &nm, &nq);
+    if (mm_supported(g)) {
+        const size_t t2 = mm_ws_bytes(g, &a, &b);
+        if (t2 > t) t = t2;
+    }
     return t;
 }
 
@@ -374,10 +401,11 @@ extern "C" int qv_rope_append(const qv_dims* d, const qv_layer* L, const void* q
     if ((cos_tab == nullptr) != (sin_tab == nullptr)) return QV_EINVAL;
     Geo g = make_geo(d);
     cudaStream_t s = (cudaStream_t)stream;
+    const dim3 grid(g.B, g.H * g.G + 2 * g.H);
     switch (g.dt) {
-        case QV_F32: rope_append_kernel<QV_F32><<<g.B, 256, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
-        case QV_BF16: rope_append_kernel<QV_BF16><<<g.B, 256, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
-        default: rope_append_kernel<QV_F16><<<g.B, 256, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
+        case QV_F32: rope_append_kernel<QV_F32><<<grid, g.D, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
+        case QV_BF16: rope_append_kernel<QV_BF16><<<grid, g.D, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
+        default: rope_append_kernel<QV_F16><<<grid, g.D, 0, s>>>(g, *L, q_in, k_in, v_in, cos_tab, sin_tab, q_out); break;
     }
     return check_launch();
 }
@@ -399,11 +427,16 @@ extern "C" int qv_decode_attention(const qv_dims* d, const qv_layer* L, const vo
     DecodeWs ws;
     decode_ws_layout(g, &op, &ol, &tot, &ws.n_main, &ws.n_q);
     if (workspace_bytes < tot) return QV_ESPACE;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (mm_supported(g)) {
+        size_t a2, b2;
+        if (workspace_bytes < mm_ws_bytes(g, &a2, &b2)) return QV_ESPACE;
+        return mm_launch(g, *L, q, out, workspace, s);
+    }
     char* base = reinterpret_cast<char*>(workspace);
     ws.tickets = reinterpret_cast<int*>(base);
     ws.partial = reinterpret_cast<float*>(base + op);
     ws.logits = base + ol;
-    cudaStream_t s = (cudaStream_t)stream;
     switch (g.dt) {
         case QV_F32: if (g.D == 128) launch_decode<QV_F32, 128>(g, *L, q, ws, out, s); else launch_decode<QV_F32, 64>(g, *L, q, ws, out, s); break;
         case QV_BF16: if (g.D == 128) launch_decode<QV_BF16, 128>(g, *L, q, ws, out, s); else launch_decode<QV_BF16, 64>(g, *L, q, ws, out, s); break;

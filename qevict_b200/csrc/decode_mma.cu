@@ -1,0 +1,821 @@
+// Decode attention, tensor-core version for the production shape
+// (head_dim 128, omega 64, sink a multiple of 64, BF16/FP16 KV, INT8 Q-cache).
+//
+// Same semantics as decode_split_kernel (decode.cu) -- see that file for the
+// reference citations -- restructured for B200:
+//
+//   * Persistent CTAs, one per SM.  The (sequence, KV head) work is flattened
+//     into equal-byte items (32-token main-zone tiles, 64-token Q-cache windows)
+//     split into contiguous ranges, one per CTA.
+//   * One producer warp streams items through a ring of shared-memory stages
+//     with 2-D TMA tiles (128-byte swizzle, no multicast) and 1-D bulk copies for
+//     the Q-cache scales; every mbarrier wait is bounded.  Items holding no live
+//     token (empty sticky / Q slots) are never fetched.
+//   * Eight consumer warps each take whole items, round-robin, and run both
+//     products on the tensor cores with the GQA group in the MMA's N dimension:
+//     S^T[tok, head] = K[tok, :] . Q^T  and  O^T[d, head] += V^T[d, tok] . P^T,
+//     P^T obtained from the S^T accumulators by movmatrix.  BF16 P is split into
+//     hi + lo halves (two MMAs) so the products carry ~16 mantissa bits of P.
+//   * INT8 Q-cache windows feed f16 MMAs directly: a code byte c becomes the
+//     f16 value 1024 + c with one byte-permute; the per-channel K scale is
+//     folded into Q, the per-token V scale into P, and the 1024 offset and the
+//     zero points are added back as per-head corrections (exact fp32
+//     dequantisation; see QV_FLAG_REFERENCE_ROUNDING for the reference's own).
+//   * Logits are rounded like the reference's (q.k rounded to the KV dtype,
+//     / sqrt(D) rounded) and written for the ledger fold; each CTA merges its
+//     warps into one partial per (sequence, head, zone).  A second kernel
+//     (decode_combine_kernel, chained with programmatic dependent launch)
+//     merges the partials, writes the output and folds the exact probabilities
+//     into the vote ledger and the Q-window scores.
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "codec.cuh"
+#include "ptx.cuh"
+
+namespace qv {
+
+constexpr int MM_CW = 8;                       // consumer warps
+constexpr int MM_THREADS = (MM_CW + 1) * 32;   // + one producer warp
+constexpr int MM_STAGE = 17408;                // bytes per stage (17 KB, 1024-aligned)
+constexpr int MM_MAXNS = 12;                   // max pipeline stages
+constexpr int MM_G = 8;                        // max GQA group
+constexpr int MM_SKIPMAP = 2048;               // items whose skip flag is cached in smem
+constexpr int MM_MT = 32;                      // tokens per main-zone item
+
+struct MmPlan {
+    int n_main;       // main items per (b, h): S_cap / 32
+    int n_q;          // Q windows per (b, h)
+    int ipb;          // items per (b, h)
+    long long total;  // items overall
+    int nC;           // CTAs (<= total, so every CTA owns at least one item)
+    int pmax;         // partial slots per (b, h, zone)
+    int ns;           // pipeline stages
+};
+
+__host__ __device__ inline int mm_cta_of(const MmPlan& P, long long i) {
+    return (int)(i * P.nC / P.total);
+}
+__host__ __device__ inline long long mm_first_item(const MmPlan& P, int c) {
+    return ((long long)c * P.total + P.nC - 1) / P.nC;  // smallest i with i * nC / total >= c
+}
+__device__ inline void mm_zone_ctas(const MmPlan& P, long long bh, int zone, int* first, int* count) {
+    const long long a = bh * P.ipb + (zone ? P.n_main : 0);
+    const long long e = bh * P.ipb + (zone ? P.ipb : P.n_main);
+    if (e <= a) { *first = 0; *count = 0; return; }
+    *first = mm_cta_of(P, a);
+    *count = mm_cta_of(P, e - 1) - *first + 1;
+}
+
+// Liveness of main-zone position pos (used by the combine kernel's fold).
+__device__ __forceinline__ bool mm_live(const Geo& g, const int32_t* swid, int pos, int cw, int tv) {
+    if (pos < g.sink) return true;
+    const int r = pos - g.sink;
+    const int slot = r / g.om;
+    if (slot < g.kw) return swid[slot] >= 0;
+    const int rs = slot - g.kw;
+    const int L0 = cw - (g.R - 1);
+    const int w = L0 + ((rs - (L0 % g.R)) % g.R + g.R) % g.R;
+    return w < cw || (r % g.om) < tv;
+}
+
+// Liveness of a token of a fetched main item without touching memory: sink and
+// sticky items are fetched only when occupied, so all their tokens are live; in
+// the ring only the unwritten tail of the current window is dead.
+__device__ __forceinline__ bool mm_item_live(const Geo& g, int pos, int cw, int tv) {
+    const int rb = g.ring_base();
+    if (pos < rb) return true;
+    const int rs = (pos - rb) >> 6;
+    const int L0 = cw - (g.R - 1);
+    const int w = L0 + ((rs - (L0 % g.R)) % g.R + g.R) % g.R;
+    return w < cw || ((pos - rb) & 63) < tv;
+}
+
+__device__ __forceinline__ bool mm_skip(const Geo& g, const qv_layer& L, const MmPlan& P, long long bh, int j) {
+    if (j >= P.n_main) return L.q_wid[bh * g.qw + (j - P.n_main)] < 0;
+    const int pos = j * MM_MT;
+    if (pos < g.sink) return false;
+    const int s = (pos - g.sink) >> 6;
+    return s < g.kw && L.sticky_wid[bh * g.kw + s] < 0;
+}
+
+template <int DT> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2<QV_BF16>(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<QV_F16>(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <int DT> __device__ __forceinline__ void mma_kv(float* c, const uint32_t* a, const uint32_t* b);
+template <> __device__ __forceinline__ void mma_kv<QV_BF16>(float* c, const uint32_t* a, const uint32_t* b) { mma_bf16(c, a, b); }
+template <> __device__ __forceinline__ void mma_kv<QV_F16>(float* c, const uint32_t* a, const uint32_t* b) { mma_f16(c, a, b); }
+
+__device__ __forceinline__ float f16r(float x) { return __half2float(__float2half_rn(x)); }
+
+// byte offset of (row, 16-byte chunk) in a 128-byte-row tile written by a
+// 128B-swizzled TMA box (the box starts on a 1024-byte boundary)
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+    return (uint32_t)(row * 128 + (((chunk ^ (row & 7)) & 7) << 4));
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// x / sqrt(128) correctly rounded in fp32: product with the rounded reciprocal,
+// then one fused correction with the exact residual (Markstein's method).
+__device__ __forceinline__ float div_sqrt128(float x) {
+    const float c = 11.313708305358887f;         // fp32 nearest to sqrt(128)
+    const float r = 0.0883883461356163f;         // fp32 nearest to 1/sqrt(128)
+    const float q0 = __fmul_rn(x, r);
+    const float res = __fmaf_rn(-q0, c, x);
+    return __fmaf_rn(res, r, q0);
+}
+
+template <int DT>
+__device__ __forceinline__ float logit_round(float dot) {
+    return rnd<DT>(div_sqrt128(rnd<DT>(dot)));
+}
+
+template <int DT>
+__global__ void __launch_bounds__(MM_THREADS, 1)
+decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const __grid_constant__ CUtensorMap tmKQ, const __grid_constant__ CUtensorMap tmVQ,
+                  Geo g, qv_layer L, const void* __restrict__ q, int* tickets, float* partial,
+                  void* logits, MmPlan P) {
+    using T = typename Elt<DT>::T;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int NS = P.ns;
+    const int G = g.G;
+    unsigned char* stages = smem;
+    float* s_q = reinterpret_cast<float*>(smem + NS * MM_STAGE);        // [8][128]
+    float* s_o = s_q + MM_G * 128;                                      // [CW][G][128]
+    float* s_m = s_o + MM_CW * G * 128;                                 // [CW][8]
+    float* s_l = s_m + MM_CW * MM_G;                                    // [CW][8]
+    uint64_t* full = reinterpret_cast<uint64_t*>(s_l + MM_CW * MM_G);
+    uint64_t* empty = full + MM_MAXNS;
+    unsigned char* s_skip = reinterpret_cast<unsigned char*>(empty + MM_MAXNS);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x;
+    const long long i0 = mm_first_item(P, c), i1 = mm_first_item(P, c + 1);
+    const size_t S_tot = (size_t)g.S_cap + (size_t)g.qw * g.om;
+    const int e = (int)sizeof(T);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    // Which of this CTA's items hold no live token (the slot tables are not
+    // written by the kernel that precedes this one, so read them before the wait).
+    for (long long i = i0 + threadIdx.x; i < i1 && i - i0 < MM_SKIPMAP; i += blockDim.x)
+        s_skip[i - i0] = mm_skip(g, L, P, i / P.ipb, (int)(i % P.ipb)) ? 1 : 0;
+    __syncthreads();
+    auto skipped = [&](long long i) -> bool {
+        return i - i0 < MM_SKIPMAP ? s_skip[i - i0] != 0 : mm_skip(g, L, P, i / P.ipb, (int)(i % P.ipb));
+    };
+    // wait for the preceding kernel (RoPE + append) before touching q or the cache
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int N0 = L.step[0];
+    const int cw = (N0 - g.sink) / g.om;
+    const int tv = (N0 - g.sink) % g.om + 1;
+
+    // --------------------------------------------------------------- producer
+    if (warp == MM_CW) {
+        if (lane == 0 && i0 < i1) {
+            prefetch_tensormap(&tmK);
+            prefetch_tensormap(&tmV);
+            prefetch_tensormap(&tmKQ);
+            prefetch_tensormap(&tmVQ);
+            int k = 0;
+            for (long long i = i0; i < i1; ++i) {
+                if (skipped(i)) continue;
+                const long long bh = i / P.ipb;
+                const int j = (int)(i % P.ipb);
+                const int s = k % NS;
+                if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
+                    set_err(L.err, QV_DERR_LAYOUT);
+                    break;
+                }
+                unsigned char* st = stages + s * MM_STAGE;
+                if (j < P.n_main) {
+                    mbar_arrive_expect_tx(&full[s], 16384);
+                    const int y = (int)(bh * g.S_cap + MM_MT * j);
+                    tma_load_2d(st, &tmK, 0, y, &full[s]);
+                    tma_load_2d(st + 4096, &tmK, 64, y, &full[s]);
+                    tma_load_2d(st + 8192, &tmV, 0, y, &full[s]);
+                    tma_load_2d(st + 12288, &tmV, 64, y, &full[s]);
+                } else {
+                    const size_t sw = (size_t)bh * g.qw + (j - P.n_main);
+                    mbar_arrive_expect_tx(&full[s], 16384 + 2 * 128 * e + 2 * 64 * e);
+                    tma_load_2d(st, &tmKQ, 0, (int)(sw * 64), &full[s]);
+                    tma_load_2d(st + 8192, &tmVQ, 0, (int)(sw * 64), &full[s]);
+                    bulk_load(st + 16384, reinterpret_cast<const char*>(L.ks) + sw * 128 * e, 128 * e, &full[s]);
+                    bulk_load(st + 16384 + 256, reinterpret_cast<const char*>(L.kz) + sw * 128 * e, 128 * e, &full[s]);
+                    bulk_load(st + 16384 + 512, reinterpret_cast<const char*>(L.vs) + sw * 64 * e, 64 * e, &full[s]);
+                    bulk_load(st + 16384 + 640, reinterpret_cast<const char*>(L.vz) + sw * 64 * e, 64 * e, &full[s]);
+                }
+                ++k;
+            }
+        }
+        return;
+    }
+
+    // --------------------------------------------------------------- consumers
+    const int gq = lane >> 2, t4 = lane & 3, mi = lane >> 3;
+    uint32_t bq[8][2];            // Q^T fragments (main zone)
+    float o[8][4];                // O^T accumulators: 8 d-tiles x (2 rows x 2 heads)
+    float m[2], ls[2], spp[2], svz[2];
+    int cur_key = -1;
+    long long cur_bh = -1;
+    int k = 0;
+    bool ok = true;
+    T* lgp = reinterpret_cast<T*>(logits);
+
+    auto reset_acc = [&]() {
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) o[dt][r] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        ls[0] = ls[1] = spp[0] = spp[1] = svz[0] = svz[1] = 0.f;
+    };
+
+    auto load_q = [&](long long bh) {
+        const int b = (int)(bh / g.H), h = (int)(bh % g.H);
+        consumer_sync();
+        for (int idx = threadIdx.x; idx < MM_G * 128; idx += MM_CW * 32) {
+            const int gi = idx >> 7, d = idx & 127;
+            s_q[idx] = gi < G ? ld<DT>(q, ((size_t)b * g.H * G + (size_t)h * G + gi) * 128 + d) : 0.f;
+        }
+        consumer_sync();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const float* qr = s_q + gq * 128 + 16 * kk + 2 * t4;
+            bq[kk][0] = pack2<DT>(qr[0], qr[1]);
+            bq[kk][1] = pack2<DT>(qr[8], qr[9]);
+        }
+    };
+
+    // Merge the warps' partials of one segment (the items of one (b, h, zone) in
+    // this CTA's range) and write it.
+    auto flush = [&](int key) {
+        const long long bh = key >> 1;
+        const int zone = key & 1;
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                ls[col] += __shfl_xor_sync(0xffffffffu, ls[col], off);
+                spp[col] += __shfl_xor_sync(0xffffffffu, spp[col], off);
+                svz[col] += __shfl_xor_sync(0xffffffffu, svz[col], off);
+            }
+        }
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+            const int hh = 2 * t4 + col;
+            if (hh < G) {
+                if (gq == 0) { s_m[warp * MM_G + hh] = m[col]; s_l[warp * MM_G + hh] = ls[col]; }
+#pragma unroll
+                for (int dt = 0; dt < 8; ++dt) {
+                    float va = o[dt][col], vb = o[dt][2 + col];
+                    int da, db;
+                    if (zone == 0) { da = 16 * dt + gq; db = da + 8; }
+                    else {
+                        da = 16 * dt + 2 * gq; db = da + 1;
+                        va = (va - 1024.f * spp[col]) * (1.f / 1024.f) + svz[col];
+                        vb = (vb - 1024.f * spp[col]) * (1.f / 1024.f) + svz[col];
+                    }
+                    s_o[(warp * G + hh) * 128 + da] = va;
+                    s_o[(warp * G + hh) * 128 + db] = vb;
+                }
+            }
+        }
+        consumer_sync();
+        int first, cnt;
+        mm_zone_ctas(P, bh, zone, &first, &cnt);
+        float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
+        for (int idx = threadIdx.x; idx < G * 128; idx += MM_CW * 32) {
+            const int hh = idx >> 7, d = idx & 127;
+            float M = -INFINITY;
+            for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, s_m[w * MM_G + hh]);
+            float acc = 0.f, lsum = 0.f;
+            if (M > -INFINITY)
+                for (int w = 0; w < MM_CW; ++w) {
+                    const float mw = s_m[w * MM_G + hh];
+                    if (mw == -INFINITY) continue;
+                    const float ew = __expf(mw - M);
+                    acc += s_o[(w * G + hh) * 128 + d] * ew;
+                    lsum += s_l[w * MM_G + hh] * ew;
+                }
+            part[hh * 130 + 2 + d] = acc;
+            if (d == 0) { part[hh * 130] = M; part[hh * 130 + 1] = lsum; }
+        }
+        consumer_sync();
+    };
+
+    // online-softmax update for one column from this lane's NV logits
+    auto softmax_update = [&](int col, const float* lgv, float* pv, int nv) {
+        float mx = -INFINITY;
+        for (int x = 0; x < nv; ++x) mx = fmaxf(mx, lgv[x]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(m[col], mx);
+        if (mn == -INFINITY) {
+            for (int x = 0; x < nv; ++x) pv[x] = 0.f;
+            return;
+        }
+        if (mn > m[col]) {
+            const float scl = __expf(m[col] - mn);
+            ls[col] *= scl;
+            spp[col] *= scl;
+            svz[col] *= scl;
+#pragma unroll
+            for (int dt = 0; dt < 8; ++dt) {
+                o[dt][col] *= scl;
+                o[dt][2 + col] *= scl;
+            }
+            m[col] = mn;
+        }
+        float sum = 0.f;
+        for (int x = 0; x < nv; ++x) {
+            pv[x] = __expf(lgv[x] - mn);
+            sum += pv[x];
+        }
+        ls[col] += sum;
+    };
+
+    for (long long i = i0; i < i1; ++i) {
+        const long long bh = i / P.ipb;
+        const int j = (int)(i % P.ipb);
+        const int zone = j >= P.n_main ? 1 : 0;
+        const int key = (int)(bh * 2 + zone);
+        if (key != cur_key) {
+            if (cur_key >= 0) flush(cur_key);
+            if (bh != cur_bh) { load_q(bh); cur_bh = bh; }
+            reset_acc();
+            cur_key = key;
+        }
+        if (skipped(i)) continue;
+        const int kk_item = k++;
+        if (kk_item % MM_CW != warp) continue;   // another warp's item
+        const int s = kk_item % NS;
+        // A warp that gives up waiting keeps walking the items (and joins every
+        // named barrier) without computing, so no barrier is left unmatched.
+        if (ok && !mbar_wait_bounded(&full[s], (kk_item / NS) & 1)) {
+            set_err(L.err, QV_DERR_LAYOUT);
+            ok = false;
+        }
+        if (!ok) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            continue;
+        }
+        const uint32_t st = smem_u32(stages + s * MM_STAGE);
+        const unsigned char* stp = stages + s * MM_STAGE;
+        if (zone == 0) {
+            // ---------------- main zone: 32 tokens = 2 m-tiles -----------------
+            float sc[2][4];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) sc[mt][r] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const int d = 16 * kk + 8 * (mi >> 1);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                    uint32_t a[4];
+                    ldsm_x4(st + (d >= 64 ? 4096 : 0) + swz(row, (d & 63) >> 3), a[0], a[1], a[2], a[3]);
+                    mma_kv<DT>(sc[mt], a, bq[kk]);
+                }
+            }
+            float lg[2][4];   // per column: [mt*2 + rowhalf]
+            const int pos0 = MM_MT * j;
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const int tA = 16 * mt + gq, tB = tA + 8;
+                const bool la = mm_item_live(g, pos0 + tA, cw, tv), lb = mm_item_live(g, pos0 + tB, cw, tv);
+                const float v0 = la ? logit_round<DT>(sc[mt][0]) : -INFINITY;
+                const float v1 = la ? logit_round<DT>(sc[mt][1]) : -INFINITY;
+                const float v2 = lb ? logit_round<DT>(sc[mt][2]) : -INFINITY;
+                const float v3 = lb ? logit_round<DT>(sc[mt][3]) : -INFINITY;
+                lg[0][2 * mt] = v0; lg[1][2 * mt] = v1; lg[0][2 * mt + 1] = v2; lg[1][2 * mt + 1] = v3;
+                const int h0 = 2 * t4;
+                const size_t ia = ((size_t)bh * S_tot + pos0 + tA) * G + h0, ib = ((size_t)bh * S_tot + pos0 + tB) * G + h0;
+                if (h0 + 1 < G) {
+                    if (la) *reinterpret_cast<uint32_t*>(lgp + ia) = pack2<DT>(v0, v1);
+                    if (lb) *reinterpret_cast<uint32_t*>(lgp + ib) = pack2<DT>(v2, v3);
+                } else if (h0 < G) {
+                    if (la) lgp[ia] = Elt<DT>::t(v0);
+                    if (lb) lgp[ib] = Elt<DT>::t(v2);
+                }
+            }
+            float p[2][4];
+            softmax_update(0, lg[0], p[0], 4);
+            softmax_update(1, lg[1], p[1], 4);
+            // P^T fragments per 16-token k-step (hi + lo halves for BF16)
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                uint32_t bp[2], bl[2];
+                bp[0] = movm_t(pack2<DT>(p[0][2 * mt], p[1][2 * mt]));
+                bp[1] = movm_t(pack2<DT>(p[0][2 * mt + 1], p[1][2 * mt + 1]));
+                if (DT == QV_BF16) {
+                    const float r0 = p[0][2 * mt] - rnd<QV_BF16>(p[0][2 * mt]);
+                    const float r1 = p[1][2 * mt] - rnd<QV_BF16>(p[1][2 * mt]);
+                    const float r2 = p[0][2 * mt + 1] - rnd<QV_BF16>(p[0][2 * mt + 1]);
+                    const float r3 = p[1][2 * mt + 1] - rnd<QV_BF16>(p[1][2 * mt + 1]);
+                    bl[0] = movm_t(pack2<DT>(r0, r1));
+                    bl[1] = movm_t(pack2<DT>(r2, r3));
+                }
+#pragma unroll
+                for (int dt = 0; dt < 8; ++dt) {
+                    const int row = 16 * mt + (lane & 7) + 8 * (mi >> 1);
+                    const int d = 16 * dt + 8 * (mi & 1);
+                    uint32_t a[4];
+                    ldsm_x4_t(st + 8192 + (d >= 64 ? 4096 : 0) + swz(row, (d & 63) >> 3), a[0], a[1], a[2], a[3]);
+                    mma_kv<DT>(o[dt], a, bp);
+                    if (DT == QV_BF16) mma_kv<DT>(o[dt], a, bl);
+                }
+            }
+        } else {
+            // ---------------- Q-cache window: 64 tokens = 4 m-tiles ------------
+            const T* ks = reinterpret_cast<const T*>(stp + 16384);
+            const T* kz = reinterpret_cast<const T*>(stp + 16384 + 256);
+            const T* vs = reinterpret_cast<const T*>(stp + 16384 + 512);
+            const T* vz = reinterpret_cast<const T*>(stp + 16384 + 640);
+            uint32_t bk[8][2];
+            float zsum = 0.f, ssum = 0.f;
+            const float* qr = s_q + gq * 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const int d0 = 16 * kk + 4 * t4;
+                float qs[4];
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const float qv = qr[d0 + jj];
+                    qs[jj] = f16r(qv * Elt<DT>::f(ks[d0 + jj]));
+                    zsum = fmaf(qv, Elt<DT>::f(kz[d0 + jj]), zsum);
+                    ssum += qs[jj];
+                }
+                bk[kk][0] = pack2<QV_F16>(qs[0], qs[1]);
+                bk[kk][1] = pack2<QV_F16>(qs[2], qs[3]);
+            }
+            zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
+            zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
+            ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
+            ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
+            const float cr = zsum - 1024.f * ssum;
+            const float corr0 = __shfl_sync(0xffffffffu, cr, 8 * t4);
+            const float corr1 = __shfl_sync(0xffffffffu, cr, 8 * t4 + 4);
+            float sc[4][4];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) sc[mt][r] = 0.f;
+#pragma unroll
+            for (int kk2 = 0; kk2 < 4; ++kk2) {
+                const int chunk = 2 * kk2 + (mi >> 1);
+#pragma unroll
+                for (int mt = 0; mt < 4; ++mt) {
+                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                    uint32_t r[4];
+                    ldsm_x4(st + swz(row, chunk), r[0], r[1], r[2], r[3]);
+                    const uint32_t a0[4] = {__byte_perm(r[0], 0x64646464u, 0x5140), __byte_perm(r[1], 0x64646464u, 0x5140),
+                                            __byte_perm(r[0], 0x64646464u, 0x5342), __byte_perm(r[1], 0x64646464u, 0x5342)};
+                    const uint32_t a1[4] = {__byte_perm(r[2], 0x64646464u, 0x5140), __byte_perm(r[3], 0x64646464u, 0x5140),
+                                            __byte_perm(r[2], 0x64646464u, 0x5342), __byte_perm(r[3], 0x64646464u, 0x5342)};
+                    mma_f16(sc[mt], a0, bk[2 * kk2]);
+                    mma_f16(sc[mt], a1, bk[2 * kk2 + 1]);
+                }
+            }
+            const int slot = j - P.n_main;
+            float lg[2][8];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int tA = 16 * mt + gq;
+                const float v0 = logit_round<DT>(sc[mt][0] + corr0);
+                const float v1 = logit_round<DT>(sc[mt][1] + corr1);
+                const float v2 = logit_round<DT>(sc[mt][2] + corr0);
+                const float v3 = logit_round<DT>(sc[mt][3] + corr1);
+                lg[0][2 * mt] = v0; lg[1][2 * mt] = v1; lg[0][2 * mt + 1] = v2; lg[1][2 * mt + 1] = v3;
+                const int h0 = 2 * t4;
+                const size_t ia = ((size_t)bh * S_tot + g.S_cap + (size_t)slot * 64 + tA) * G + h0;
+                const size_t ib = ia + 8 * (size_t)G;
+                if (h0 + 1 < G) {
+                    *reinterpret_cast<uint32_t*>(lgp + ia) = pack2<DT>(v0, v1);
+                    *reinterpret_cast<uint32_t*>(lgp + ib) = pack2<DT>(v2, v3);
+                } else if (h0 < G) {
+                    lgp[ia] = Elt<DT>::t(v0);
+                    lgp[ib] = Elt<DT>::t(v2);
+                }
+            }
+            float p[2][8];
+            softmax_update(0, lg[0], p[0], 8);
+            softmax_update(1, lg[1], p[1], 8);
+            uint32_t bp[4][2];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int tA = 16 * mt + gq, tB = tA + 8;
+                const float vsA = Elt<DT>::f(vs[tA]) * 1024.f, vsB = Elt<DT>::f(vs[tB]) * 1024.f;
+                const float vzA = Elt<DT>::f(vz[tA]), vzB = Elt<DT>::f(vz[tB]);
+                // P'' = p * v_scale * 1024 in f16; corrections use the rounded values
+                const float pa0 = f16r(p[0][2 * mt] * vsA), pa1 = f16r(p[1][2 * mt] * vsA);
+                const float pb0 = f16r(p[0][2 * mt + 1] * vsB), pb1 = f16r(p[1][2 * mt + 1] * vsB);
+                spp[0] += pa0 + pb0;
+                spp[1] += pa1 + pb1;
+                svz[0] += p[0][2 * mt] * vzA + p[0][2 * mt + 1] * vzB;
+                svz[1] += p[1][2 * mt] * vzA + p[1][2 * mt + 1] * vzB;
+                bp[mt][0] = movm_t(pack2<QV_F16>(pa0, pa1));
+                bp[mt][1] = movm_t(pack2<QV_F16>(pb0, pb1));
+            }
+#pragma unroll
+            for (int dt2 = 0; dt2 < 4; ++dt2) {
+                const int chunk = 2 * dt2 + (mi >> 1);
+#pragma unroll
+                for (int mt = 0; mt < 4; ++mt) {
+                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                    uint32_t r[4];
+                    ldsm_x4_t(st + 8192 + swz(row, chunk), r[0], r[1], r[2], r[3]);
+                    const uint32_t a0[4] = {__byte_perm(r[0], 0x64646464u, 0x5240), __byte_perm(r[0], 0x64646464u, 0x5341),
+                                            __byte_perm(r[1], 0x64646464u, 0x5240), __byte_perm(r[1], 0x64646464u, 0x5341)};
+                    const uint32_t a1[4] = {__byte_perm(r[2], 0x64646464u, 0x5240), __byte_perm(r[2], 0x64646464u, 0x5341),
+                                            __byte_perm(r[3], 0x64646464u, 0x5240), __byte_perm(r[3], 0x64646464u, 0x5341)};
+                    mma_f16(o[2 * dt2], a0, bp[mt]);
+                    mma_f16(o[2 * dt2 + 1], a1, bp[mt]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (cur_key >= 0) flush(cur_key);
+    // let the combine grid get scheduled while this grid drains (it waits for
+    // this grid's completion before reading anything)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // every CTA has read the token counter at its start; the last one to finish
+    // advances it (the combine kernel reads the advanced value)
+    __threadfence();
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(tickets, 1) == (int)gridDim.x - 1) {
+            tickets[0] = 0;
+            L.step[0] = N0 + 1;
+        }
+    }
+}
+
+// Merge the per-CTA partials of one (sequence, KV head), write the output, and
+// fold the exact probabilities of a chunk of its tokens into the vote ledger /
+// Q-window scores.  grid = (chunks, B*H); chunk 0 also writes the output.
+template <int DT>
+__global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, void* __restrict__ out,
+                                                             const float* __restrict__ partial,
+                                                             const void* __restrict__ logits, MmPlan P,
+                                                             int blocks_per_chunk) {
+    // 64-token blocks of this (b, h): main zone blocks, then one per Q window
+    const int n_mblk = g.S_cap / 64;
+    const int n_blk = n_mblk + g.qw;
+    // wait for the streaming kernel (programmatic dependent launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    constexpr int MAXP = 64;
+    __shared__ float s_m[MM_G][2 * MAXP];
+    __shared__ float s_w[MM_G][2 * MAXP];
+    __shared__ float s_l[MM_G][2 * MAXP];
+    __shared__ float s_M[MM_G], s_L[MM_G];
+    const long long bh = blockIdx.y;
+    const int b = (int)(bh / g.H), h = (int)(bh % g.H);
+    const int G = g.G;
+    const int N0 = L.step[0] - 1;
+    const int cw = (N0 - g.sink) / g.om;
+    const int tv = (N0 - g.sink) % g.om + 1;
+    const size_t S_tot = (size_t)g.S_cap + (size_t)g.qw * g.om;
+    int f0, c0, f1, c1;
+    mm_zone_ctas(P, bh, 0, &f0, &c0);
+    mm_zone_ctas(P, bh, 1, &f1, &c1);
+    const int np = c0 + c1;
+    const float* pz[2] = {partial + ((size_t)bh * 2 + 0) * P.pmax * G * 130,
+                          partial + ((size_t)bh * 2 + 1) * P.pmax * G * 130};
+    for (int t = threadIdx.x; t < G * np; t += blockDim.x) {
+        const int hh = t / np, s = t % np;
+        const float* pr = s < c0 ? pz[0] + (size_t)s * G * 130 + hh * 130 : pz[1] + (size_t)(s - c0) * G * 130 + hh * 130;
+        s_m[hh][s] = pr[0];
+        s_l[hh][s] = pr[1];
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int hh = threadIdx.x;
+        float M = -INFINITY;
+        for (int s = 0; s < np; ++s) M = fmaxf(M, s_m[hh][s]);
+        float Ls = 0.f;
+        for (int s = 0; s < np; ++s)
+            if (s_m[hh][s] > -INFINITY) Ls += s_l[hh][s] * expf(s_m[hh][s] - M);
+        s_M[hh] = M;
+        s_L[hh] = Ls;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < G * np; t += blockDim.x) {
+        const int hh = t / np, s = t % np;
+        s_w[hh][s] = s_m[hh][s] > -INFINITY ? expf(s_m[hh][s] - s_M[hh]) : 0.f;
+    }
+    __syncthreads();
+    // this CTA's slice of the G*128 output elements; (element, partial) products
+    // are spread over all threads and reduced in shared memory
+    {
+        __shared__ float s_acc[2][MM_G * 128];
+        const int ne = G * 128;
+        const int per = (ne + gridDim.x - 1) / gridDim.x;
+        const int e0 = blockIdx.x * per, e1 = min(e0 + per, ne);
+        for (int t = threadIdx.x; t < 2 * (e1 - e0); t += blockDim.x) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
+        __syncthreads();
+        const int work = (e1 - e0) * np;
+        for (int t = threadIdx.x; t < work; t += blockDim.x) {
+            const int el = e0 + t / np, s = t % np;
+            const int hh = el >> 7, d = el & 127;
+            const float* pr = s < c0 ? pz[0] + (size_t)s * G * 130 : pz[1] + (size_t)(s - c0) * G * 130;
+            atomicAdd(&s_acc[s < c0 ? 0 : 1][el], pr[hh * 130 + 2 + d] * s_w[hh][s]);
+        }
+        __syncthreads();
+        const bool has_q = L.seq[b * 4 + 1] > 0;
+        for (int el = e0 + threadIdx.x; el < e1; el += blockDim.x) {
+            const int hh = el >> 7, d = el & 127;
+            const float inv = 1.f / s_L[hh];
+            const float om_ = s_acc[0][el], oq = s_acc[1][el];
+            const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
+            st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
+        }
+    }
+    // this chunk's 64-token blocks: main tiles first, then Q windows
+    const int blk0 = blockIdx.x * blocks_per_chunk;
+    const int blk1 = min(blk0 + blocks_per_chunk, n_blk);
+    const int32_t* swid = L.sticky_wid + bh * g.kw;
+    const int32_t* qwid = L.q_wid + bh * g.qw;
+    using T = typename Elt<DT>::T;
+    const T* lg = reinterpret_cast<const T*>(logits);
+    const int main_end = min(blk1, n_mblk) * 64;
+    for (int pos = blk0 * 64 + threadIdx.x; pos < main_end; pos += blockDim.x) {
+        if (!mm_live(g, swid, pos, cw, tv)) continue;
+        const T* row = lg + ((size_t)bh * S_tot + pos) * G;
+        float acc = 0.f;
+        for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(expf(Elt<DT>::f(row[hh]) - s_M[hh]) / s_L[hh]);
+        L.votes[bh * g.S_cap + pos] += rnd<DT>(acc / (float)G);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int blk = max(blk0, n_mblk) + warp; blk < blk1; blk += blockDim.x >> 5) {
+        const int slot = blk - n_mblk;
+        if (qwid[slot] < 0) continue;
+        float a = 0.f;
+        bool first = true;
+        for (int t = lane; t < 64; t += 32) {
+            const T* row = lg + ((size_t)bh * S_tot + g.S_cap + (size_t)slot * 64 + t) * G;
+            float acc = 0.f;
+            for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(expf(Elt<DT>::f(row[hh]) - s_M[hh]) / s_L[hh]);
+            const float mean = rnd<DT>(acc / (float)G);
+            a = first ? mean : a + mean;
+            first = false;
+        }
+        a = warp_sum(a);
+        if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+static bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t inner, uint64_t rows,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+    }
+    return n;
+}
+
+bool mm_supported(const Geo& g) {
+    return !(g.flags & QV_FLAG_REFERENCE_ROUNDING) && (g.dt == QV_BF16 || g.dt == QV_F16) && g.D == 128 &&
+           g.om == 64 && g.sink % 64 == 0 && g.bits == 8 && g.G <= MM_G && g.S_cap % 64 == 0;
+}
+
+static size_t mm_fixed_smem(const Geo& g) {
+    return 1024 + (size_t)(MM_G * 128 + MM_CW * g.G * 128 + 2 * MM_CW * MM_G) * 4 + 2 * MM_MAXNS * 8 + MM_SKIPMAP;
+}
+
+MmPlan mm_plan(const Geo& g) {
+    MmPlan P;
+    P.n_main = g.S_cap / MM_MT;
+    P.n_q = g.qw;
+    P.ipb = P.n_main + P.n_q;
+    P.total = (long long)P.ipb * g.B * g.H;
+    long long nc = sm_count();
+    if (nc > P.total) nc = P.total;
+    P.nC = (int)(nc < 1 ? 1 : nc);
+    const long long wz = P.n_main > P.n_q ? P.n_main : P.n_q;
+    P.pmax = (int)((wz * P.nC + P.total - 1) / P.total + 2);
+    int ns = (int)((232448 - mm_fixed_smem(g)) / MM_STAGE);
+    P.ns = ns > MM_MAXNS ? MM_MAXNS : ns;
+    return P;
+}
+
+size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
+    MmPlan P = mm_plan(g);
+    const size_t BH = (size_t)g.B * g.H;
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    size_t o = al((BH + 1) * sizeof(int));
+    *off_part = o;
+    o += al(BH * 2 * P.pmax * g.G * 130 * sizeof(float));
+    *off_logits = o;
+    o += al(BH * (size_t)(g.S_cap + g.qw * g.om) * g.G * elt_size(g.dt));
+    return o;
+}
+
+int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s) {
+    MmPlan P = mm_plan(g);
+    if (P.pmax > 64 || P.ns < 2) return QV_EINVAL;
+    size_t op, ol;
+    mm_ws_bytes(g, &op, &ol);
+    char* base = reinterpret_cast<char*>(ws);
+    CUtensorMap mk, mv, mkq, mvq;
+    const CUtensorMapDataType kt = g.dt == QV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t rows = (uint64_t)g.B * g.H * g.S_cap;
+    const uint64_t qrows = (uint64_t)g.B * g.H * (g.qw > 0 ? g.qw : 1) * 64;
+    bool okm = make_map(&mk, L.k, kt, 128, rows, 256, 64, MM_MT) && make_map(&mv, L.v, kt, 128, rows, 256, 64, MM_MT);
+    const void* kqb = g.qw > 0 ? (const void*)L.kq : (const void*)L.k;
+    const void* vqb = g.qw > 0 ? (const void*)L.vq : (const void*)L.v;
+    okm = okm && make_map(&mkq, kqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64) &&
+          make_map(&mvq, vqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64);
+    if (!okm) return QV_EINVAL;
+    const size_t smem = mm_fixed_smem(g) + (size_t)P.ns * MM_STAGE;
+    static int cached[3] = {48 * 1024, 48 * 1024, 48 * 1024};
+    int* tickets = reinterpret_cast<int*>(base);
+    float* part = reinterpret_cast<float*>(base + op);
+    void* lgt = base + ol;
+    const int BH = g.B * g.H;
+    const int n_blk = g.S_cap / 64 + g.qw;
+    int chunks = (2 * sm_count() + BH - 1) / BH;
+    if (chunks > n_blk) chunks = n_blk;
+    if (chunks < 1) chunks = 1;
+    const int bpc = (n_blk + chunks - 1) / chunks;
+    chunks = (n_blk + bpc - 1) / bpc;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg1 = {};
+    cfg1.gridDim = dim3(P.nC);
+    cfg1.blockDim = dim3(MM_THREADS);
+    cfg1.dynamicSmemBytes = smem;
+    cfg1.stream = s;
+    cfg1.attrs = attr;
+    cfg1.numAttrs = 1;
+    cudaLaunchConfig_t cfg2 = cfg1;
+    cfg2.gridDim = dim3(chunks, BH);
+    cfg2.blockDim = dim3(256);
+    cfg2.dynamicSmemBytes = 0;
+    cudaError_t e;
+    if (g.dt == QV_BF16) {
+        e = ensure_smem(decode_mma_kernel<QV_BF16>, smem, &cached[1]);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        e = cudaLaunchKernelEx(&cfg1, decode_mma_kernel<QV_BF16>, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        e = cudaLaunchKernelEx(&cfg2, decode_combine_kernel<QV_BF16>, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
+    } else {
+        e = ensure_smem(decode_mma_kernel<QV_F16>, smem, &cached[2]);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        e = cudaLaunchKernelEx(&cfg1, decode_mma_kernel<QV_F16>, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        e = cudaLaunchKernelEx(&cfg2, decode_combine_kernel<QV_F16>, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
+    }
+    if (e != cudaSuccess) return set_cuda_error(e);
+    return check_launch();
+}
+
+}  // namespace qv

@@ -55,7 +55,8 @@ class Workspace:
 
 class StickyLayerState:
     def __init__(self, batch, kv_heads, group, head_dim, omega, sink, local, k_windows, q_windows,
-                 max_windows, bits=8, dtype=torch.bfloat16, device="cuda", workspace=None):
+                 max_windows, bits=8, dtype=torch.bfloat16, device="cuda", workspace=None,
+                 reference_rounding=False):
         if local % omega or local < omega:
             raise N.QevictError("the local zone must be a positive whole number of windows")
         self.B, self.H, self.G, self.D = batch, kv_heads, group, head_dim
@@ -64,10 +65,14 @@ class StickyLayerState:
         self.dtype = dtype
         self.device = torch.device(device)
         self.dims = N.QvDims(batch, kv_heads, group, head_dim, omega, sink, local, k_windows,
-                             q_windows, max_windows, bits, kv_dtype_code(dtype))
+                             q_windows, max_windows, bits, kv_dtype_code(dtype),
+                             N.QV_FLAG_REFERENCE_ROUNDING if reference_rounding else 0)
         lib = N.lib()
         self.R = int(lib.qv_ring_windows(ctypes.byref(self.dims)))
         self.S_cap = int(lib.qv_main_capacity(ctypes.byref(self.dims)))
+        # 1: tensor-core decode (exact fp32 dequantisation of the Q-cache);
+        # 0: CUDA-core decode with the reference's dequantisation rounding
+        self.decode_path = int(lib.qv_decode_path(ctypes.byref(self.dims)))
         if self.R < 0 or self.S_cap < 0:
             raise N.QevictError("invalid layer dimensions for the native library")
         B, H, D, om, dev = batch, kv_heads, head_dim, omega, self.device
@@ -223,6 +228,25 @@ class StickyLayerState:
         pos = self.reference_positions(b)
         idx = pos[:, :, None].expand(-1, -1, self.D)
         return (torch.gather(self.k[b], 1, idx).float().cpu(), torch.gather(self.v[b], 1, idx).float().cpu())
+
+    def view_logits(self, b):
+        """Rounded logits of the last decode step, [H, G, S_ref + Q tokens] in the
+        reference's order (main zone as reference_positions, then Q windows in
+        top-k order), as float32 on CPU."""
+        off = int(N.lib().qv_decode_logits_offset(ctypes.byref(self.dims)))
+        S_tot = self.S_cap + self.qw * self.omega
+        n = self.B * self.H * S_tot * self.G
+        lg = self.ws.decode[off:off + n * self.k.element_size()].view(self.dtype)
+        lg = lg.view(self.B, self.H, S_tot, self.G)[b]
+        pos = self.reference_positions(b)                          # [H, S_ref]
+        main = torch.gather(lg, 1, pos[:, :, None].expand(-1, -1, self.G))
+        parts = [main]
+        qc = self.counts()[1][b]
+        if qc:
+            o = self.q_order[b, :, :qc].long()
+            qpos = self.S_cap + (o[:, :, None] * self.omega + torch.arange(self.omega, device=self.device)).reshape(self.H, -1)
+            parts.append(torch.gather(lg, 1, qpos[:, :, None].expand(-1, -1, self.G)))
+        return torch.cat(parts, dim=1).permute(0, 2, 1).float().cpu()
 
     def view_votes(self, b):
         pos = self.reference_positions(b)

@@ -1,0 +1,108 @@
+"""Decode-attention microbenchmark at Llama-3-8B layer shape.
+
+One Sticky-KV layer (8 KV heads, GQA group 4, head_dim 128, bf16) for B
+sequences, state built from a random prompt through the prefill state builder,
+then decode steps of RoPE + append, the fused attention with the ledger fold,
+and the eviction cycle every omega tokens.  Inputs are random; per-step
+device time is taken with CUDA events on the launching stream (the stream is
+kept busy while the host issues each launch, so the events bracket device
+time only).
+
+Default sizes are the decode microbenchmark configuration: batch 64,
+per-sequence cache of 64 sink + 512 local + 2048 sticky BF16 tokens and 4096
+INT8 Q-cache tokens, 1000 steps.
+
+    python -m qevict_b200.microbench [--batch 64] [--steps 1000] [--sticky 32] [--qwin 64]
+"""
+
+import argparse
+import json
+
+import torch
+
+from .layer_state import StickyLayerState
+
+H, G, D, OMEGA, SINK = 8, 4, 128, 64, 64
+
+
+def algorithmic_bytes(batch, sticky, qwin, local, t, e=2, qbytes=128):
+    """HBM bytes one attention launch must read: BF16 K+V of the live main zone,
+    INT8 K+V codes + per-token V scale/zp + per-window K scale/zp of the Q-cache."""
+    s_m = SINK + sticky * OMEGA + local + t
+    s_q = qwin * OMEGA
+    return batch * H * (s_m * 2 * D * e + s_q * (2 * qbytes + 2 * e) + qwin * 2 * D * e)
+
+
+def build(batch, sticky, qwin, local, seed=0, dtype=torch.bfloat16):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    st = StickyLayerState(batch, H, G, D, OMEGA, SINK, local, sticky, qwin, 4096, 8, dtype)
+    prompt = SINK + (sticky + qwin) * OMEGA + local
+    k = torch.randn(batch, H, prompt, D, generator=g, device="cuda").to(dtype)
+    v = torch.randn(batch, H, prompt, D, generator=g, device="cuda").to(dtype)
+    cs = torch.rand(batch, H, prompt, generator=g, device="cuda") * 4
+    st.prefill(k, v, cs)
+    del k, v, cs
+    torch.cuda.synchronize()
+    return st, g
+
+
+def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=False):
+    st, g = build(batch, sticky, qwin, local)
+    q = torch.randn(batch, H * G, D, generator=g, device="cuda").to(st.dtype) * 0.3
+    kn = torch.randn(batch, H, D, generator=g, device="cuda").to(st.dtype)
+    vn = torch.randn(batch, H, D, generator=g, device="cuda").to(st.dtype)
+    out = torch.empty(batch, H * G, D, dtype=st.dtype, device="cuda")
+    for _ in range(warmup):
+        st.step(q, kn, vn, out=out)
+    torch.cuda.synchronize()
+    attn_t, cyc_t, step_t, tvals = [], [], [], []
+    for _ in range(steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda._sleep(100000)
+        ev[0].record()
+        qr = st.append(q, kn, vn)
+        ev[1].record()
+        st.attend(qr, out)
+        ev[2].record()
+        t = (st.n_tokens - st.prompt_len - 1) % st.omega + 1
+        cyc = st.cycle_due()
+        if cyc:
+            st.evict_cycle()
+        ev[3].record()
+        tvals.append(t)
+        step_t.append(ev)
+    torch.cuda.synchronize()
+    for ev, t in zip(step_t, tvals):
+        attn_t.append(ev[1].elapsed_time(ev[2]) * 1e-3)
+        cyc_t.append(ev[2].elapsed_time(ev[3]) * 1e-3)
+    n_cyc = sum(1 for t in tvals if t == OMEGA)
+    by = [algorithmic_bytes(batch, sticky, qwin, local, t) for t in tvals]
+    avg_attn = sum(attn_t) / len(attn_t)
+    res = {
+        "batch": batch, "steps": steps, "avg_attention_us": avg_attn * 1e6,
+        "attention_GBps": sum(by) / sum(attn_t) / 1e9,
+        "avg_bytes_per_launch": sum(by) / len(by),
+        "cycle_us_avg": (sum(c for c, t in zip(cyc_t, tvals) if t == OMEGA) / max(1, n_cyc)) * 1e6,
+        "cycle_fraction_of_step": (sum(cyc_t) / max(1e-12, sum(attn_t) + sum(cyc_t))),
+        "decode_path": st.decode_path, "error_word": st.read_error(),
+    }
+    if not quiet:
+        print(json.dumps(res))
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--sticky", type=int, default=32)
+    ap.add_argument("--qwin", type=int, default=64)
+    ap.add_argument("--local", type=int, default=512)
+    a = ap.parse_args()
+    run(a.batch, a.steps, a.warmup, a.sticky, a.qwin, a.local)
+
+
+if __name__ == "__main__":
+    main()

@@ -69,7 +69,7 @@ def prefill_attention(q, k, v, colsum=True):
     q [B, S, Hq, D], k/v [B, S, H, D] contiguous -> (out [B, S, Hq, D], colsum [B, H, S] fp32)."""
     B, S, Hq, D = q.shape
     H = k.shape[2]
-    dims = N.QvDims(B, H, Hq // H, D, 64, 0, 64, 0, 0, 1, 8, kv_dtype_code(q.dtype))
+    dims = N.QvDims(B, H, Hq // H, D, 64, 0, 64, 0, 0, 1, 8, kv_dtype_code(q.dtype), 0)
     import ctypes
     wsb = int(N.lib().qv_prefill_workspace_bytes(ctypes.byref(dims), S))
     ws = torch.empty(wsb, dtype=torch.uint8, device=q.device)
