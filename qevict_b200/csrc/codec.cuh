@@ -47,6 +47,7 @@ __device__ void quantize_k_window(const void* x, size_t xbase, int om, int D, in
             mn = 0.f; mx = 0.f;
         } else {
             mn = INFINITY; mx = -INFINITY;
+#pragma unroll 8
             for (int t = 0; t < om; ++t) {
                 float v = ld<DT>(x, xbase + (size_t)t * D + d);
                 mn = fminf(mn, v); mx = fmaxf(mx, v);
@@ -78,6 +79,7 @@ __device__ void quantize_k_window(const void* x, size_t xbase, int om, int D, in
         st<DT>(kz, sbase + d, s_zp[d]);
     }
     const int qb = bits == 4 ? D / 2 : D;
+#pragma unroll 4
     for (int i = threadIdx.x; i < om * qb; i += blockDim.x) {
         int t = i / qb, j = i % qb;
         if (bits == 8) {
@@ -133,6 +135,7 @@ __device__ void quantize_v_window(const void* x, size_t xbase, int om, int D, in
     }
     __syncthreads();
     const int qb = bits == 4 ? D / 2 : D;
+#pragma unroll 4
     for (int i = threadIdx.x; i < om * qb; i += blockDim.x) {
         int t = i / qb, j = i % qb;
         if (bits == 8) {

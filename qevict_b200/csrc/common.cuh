@@ -86,6 +86,7 @@ int set_cuda_error(cudaError_t e);
 int check_launch();
 
 size_t elt_size(int dt);
+__host__ __device__ constexpr size_t elt_size_dev(int dt) { return dt == QV_F32 ? 4 : 2; }
 
 // Warp reductions.
 __device__ __forceinline__ float warp_sum(float x) {

@@ -97,14 +97,35 @@ __global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, C
     float* lhist = L.local_hist + bh * g.maxW;
     uint8_t* arch = L.arch_valid + bh * g.maxW;
 
-    // 1. scoreboard over slots (eviction_manager.py:229-255)
-    for (int s = 0; s < g.kw; ++s) {
-        float v = swid[s] >= 0 ? window_tree_sum(votes + g.sink + s * g.om, g.om, lane) : 0.f;
-        if (lane == 0) sb_st[s] = v;
-    }
-    for (int r = 0; r < g.R; ++r) {
-        float v = window_tree_sum(votes + g.ring_base() + r * g.om, g.om, lane);
-        if (lane == 0) sb_ring[r] = v;
+    // 1. scoreboard over slots (eviction_manager.py:229-255): every window's votes
+    //    summed in the fixed warp order, 8 windows' loads in flight at a time
+    {
+        const int nslot = g.kw + g.R;
+        for (int s0 = 0; s0 < nslot; s0 += 8) {
+            float a[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int s = s0 + u;
+                a[u] = 0.f;
+                if (s < nslot && (s >= g.kw || swid[s] >= 0)) {
+                    const float* v = votes + g.sink + s * g.om;   // ring slots follow the sticky slots
+                    bool first = true;
+                    for (int i = lane; i < g.om; i += 32) {
+                        a[u] = first ? v[i] : a[u] + v[i];
+                        first = false;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float t = warp_sum(a[u]);
+                const int s = s0 + u;
+                if (lane == 0 && s < nslot) {
+                    if (s < g.kw) sb_st[s] = t;
+                    else sb_ring[s - g.kw] = t;
+                }
+            }
+        }
     }
     __syncwarp();
     auto sbv = [&](int w) -> float {
@@ -284,9 +305,12 @@ __global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, C
         }
         plan[0] = n_up;
         plan[1] = n_down;
-        // local history (eviction_manager.py:347-356, 398-412)
+    }
+    __syncwarp();
+    // local history (eviction_manager.py:347-356, 398-412), one window per lane
+    {
         const int start = has ? last + 1 : max(0, lnum / g.om);
-        for (int w = start; w < start + (g.R - 1); ++w)
+        for (int w = start + lane; w < start + (g.R - 1); w += 32)
             if (w >= 0 && w < g.maxW) lhist[w] += sbv(w);
     }
     __syncwarp();
@@ -317,6 +341,15 @@ __global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, C
     }
 }
 
+// 16-byte vector copy of n bytes (n a multiple of 16, both pointers 16-byte aligned)
+__device__ __forceinline__ void copy16(void* dst, const void* src, size_t n) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    const size_t n4 = n / 16;
+#pragma unroll 4
+    for (size_t i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = s4[i];
+}
+
 template <int DT>
 __global__ void __launch_bounds__(128) cycle_up_gather_kernel(Geo g, qv_layer L, CycleWs ws) {
     const size_t bh = blockIdx.x;
@@ -326,23 +359,28 @@ __global__ void __launch_bounds__(128) cycle_up_gather_kernel(Geo g, qv_layer L,
     const int* e = plan + 2 + 4 * i;
     const int kind = e[0], src = e[1], wid = e[3];
     const int om = g.om, D = g.D;
-    const size_t stK = ((bh * ws.max_up + i) * 2 + 0) * (size_t)om * D;
-    const size_t stV = stK + (size_t)om * D;
+    const size_t es = elt_size_dev(DT);
+    char* stage = reinterpret_cast<char*>(ws.staging);
+    char* stK = stage + ((bh * ws.max_up + i) * 2 + 0) * (size_t)om * D * es;
+    char* stV = stK + (size_t)om * D * es;
     const int qb = g.bits == 4 ? D / 2 : D;
-    for (int idx = threadIdx.x; idx < om * D; idx += blockDim.x) {
-        const int t = idx / D, d = idx % D;
-        float kv = 0.f, vv = 0.f;
-        if (kind == UP_PROMOTE) {
-            const size_t sw = bh * g.qw + src;
-            kv = dequant1<DT>(code_at(L.kq + (sw * om + t) * qb, d, g.bits), ld<DT>(L.ks, sw * D + d), ld<DT>(L.kz, sw * D + d));
-            vv = dequant1<DT>(code_at(L.vq + (sw * om + t) * qb, d, g.bits), ld<DT>(L.vs, sw * om + t), ld<DT>(L.vz, sw * om + t));
-        } else if (kind == UP_RING) {
-            const size_t row = (bh * g.S_cap + g.ring_base() + (size_t)src * om + t) * D + d;
-            kv = ld<DT>(L.k, row);
-            vv = ld<DT>(L.v, row);
+    if (kind == UP_RING) {
+        const size_t row = (bh * g.S_cap + g.ring_base() + (size_t)src * om) * D * es;
+        copy16(stK, reinterpret_cast<const char*>(L.k) + row, (size_t)om * D * es);
+        copy16(stV, reinterpret_cast<const char*>(L.v) + row, (size_t)om * D * es);
+    } else if (kind == UP_PROMOTE) {
+        const size_t sw = bh * g.qw + src;
+#pragma unroll 4
+        for (int idx = threadIdx.x; idx < om * D; idx += blockDim.x) {
+            const int t = idx / D, d = idx % D;
+            st<DT>(stK, idx, dequant1<DT>(code_at(L.kq + (sw * om + t) * qb, d, g.bits), ld<DT>(L.ks, sw * D + d), ld<DT>(L.kz, sw * D + d)));
+            st<DT>(stV, idx, dequant1<DT>(code_at(L.vq + (sw * om + t) * qb, d, g.bits), ld<DT>(L.vs, sw * om + t), ld<DT>(L.vz, sw * om + t)));
         }
-        st<DT>(ws.staging, stK + idx, kv);
-        st<DT>(ws.staging, stV + idx, vv);
+    } else {
+        for (int idx = threadIdx.x; idx < om * D; idx += blockDim.x) {
+            st<DT>(stK, idx, 0.f);
+            st<DT>(stV, idx, 0.f);
+        }
     }
     if (kind == UP_PROMOTE && wid >= 0 && wid < g.maxW) {
         const size_t sw = bh * g.qw + src;
@@ -389,13 +427,13 @@ __global__ void __launch_bounds__(128) cycle_up_scatter_kernel(Geo g, qv_layer L
     const int* e = plan + 2 + 4 * i;
     const int dst = e[2];
     const int om = g.om, D = g.D;
-    const size_t stK = ((bh * ws.max_up + i) * 2 + 0) * (size_t)om * D;
-    const size_t stV = stK + (size_t)om * D;
-    const size_t row0 = (bh * g.S_cap + g.sink + (size_t)dst * om) * D;
-    for (int idx = threadIdx.x; idx < om * D; idx += blockDim.x) {
-        st<DT>(L.k, row0 + idx, ld<DT>(ws.staging, stK + idx));
-        st<DT>(L.v, row0 + idx, ld<DT>(ws.staging, stV + idx));
-    }
+    const size_t es = elt_size_dev(DT);
+    const char* stage = reinterpret_cast<const char*>(ws.staging);
+    const char* stK = stage + ((bh * ws.max_up + i) * 2 + 0) * (size_t)om * D * es;
+    const char* stV = stK + (size_t)om * D * es;
+    const size_t row0 = (bh * g.S_cap + g.sink + (size_t)dst * om) * D * es;
+    copy16(reinterpret_cast<char*>(L.k) + row0, stK, (size_t)om * D * es);
+    copy16(reinterpret_cast<char*>(L.v) + row0, stV, (size_t)om * D * es);
 }
 
 }  // namespace qv

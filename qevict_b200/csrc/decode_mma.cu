@@ -192,10 +192,12 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             prefetch_tensormap(&tmKQ);
             prefetch_tensormap(&tmVQ);
             int k = 0;
+            long long bh = i0 / P.ipb;
+            int j = (int)(i0 % P.ipb) - 1;
+#pragma unroll 1
             for (long long i = i0; i < i1; ++i) {
+                if (++j == P.ipb) { j = 0; ++bh; }
                 if (skipped(i)) continue;
-                const long long bh = i / P.ipb;
-                const int j = (int)(i % P.ipb);
                 const int s = k % NS;
                 if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
                     set_err(L.err, QV_DERR_LAYOUT);
@@ -350,13 +352,19 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         ls[col] += sum;
     };
 
-    for (long long i = i0; i < i1; ++i) {
-        const long long bh = i / P.ipb;
-        const int j = (int)(i % P.ipb);
+    long long bh_it = i0 / P.ipb;
+    int j_it = (int)(i0 % P.ipb);
+#pragma unroll 1
+    for (long long i = i0;; ++i) {
+        const bool end = i >= i1;
+        const long long bh = bh_it;
+        const int j = j_it;
+        if (++j_it == P.ipb) { j_it = 0; ++bh_it; }
         const int zone = j >= P.n_main ? 1 : 0;
-        const int key = (int)(bh * 2 + zone);
+        const int key = end ? -2 : (int)(bh * 2 + zone);
         if (key != cur_key) {
             if (cur_key >= 0) flush(cur_key);
+            if (end) break;
             if (bh != cur_bh) { load_q(bh); cur_bh = bh; }
             reset_acc();
             cur_key = key;
@@ -555,7 +563,6 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (cur_key >= 0) flush(cur_key);
     // let the combine grid get scheduled while this grid drains (it waits for
     // this grid's completion before reading anything)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -615,14 +622,14 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, 
         for (int s = 0; s < np; ++s) M = fmaxf(M, s_m[hh][s]);
         float Ls = 0.f;
         for (int s = 0; s < np; ++s)
-            if (s_m[hh][s] > -INFINITY) Ls += s_l[hh][s] * expf(s_m[hh][s] - M);
+            if (s_m[hh][s] > -INFINITY) Ls += s_l[hh][s] * __expf(s_m[hh][s] - M);
         s_M[hh] = M;
         s_L[hh] = Ls;
     }
     __syncthreads();
     for (int t = threadIdx.x; t < G * np; t += blockDim.x) {
         const int hh = t / np, s = t % np;
-        s_w[hh][s] = s_m[hh][s] > -INFINITY ? expf(s_m[hh][s] - s_M[hh]) : 0.f;
+        s_w[hh][s] = s_m[hh][s] > -INFINITY ? __expf(s_m[hh][s] - s_M[hh]) : 0.f;
     }
     __syncthreads();
     // this CTA's slice of the G*128 output elements; (element, partial) products
@@ -659,11 +666,25 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, 
     using T = typename Elt<DT>::T;
     const T* lg = reinterpret_cast<const T*>(logits);
     const int main_end = min(blk1, n_mblk) * 64;
+    const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
     for (int pos = blk0 * 64 + threadIdx.x; pos < main_end; pos += blockDim.x) {
-        if (!mm_live(g, swid, pos, cw, tv)) continue;
+        const int blk = pos >> 6;
+        bool live;
+        if (blk < sink_blk) live = true;
+        else if (blk < ring_blk) live = swid[blk - sink_blk] >= 0;
+        else live = mm_live(g, swid, pos, cw, tv);
+        if (!live) continue;
         const T* row = lg + ((size_t)bh * S_tot + pos) * G;
+        float lv[MM_G];
+        if (G == 4) {
+            const uint2 u = *reinterpret_cast<const uint2*>(row);
+            const T* t = reinterpret_cast<const T*>(&u);
+            for (int hh = 0; hh < 4; ++hh) lv[hh] = Elt<DT>::f(t[hh]);
+        } else {
+            for (int hh = 0; hh < G; ++hh) lv[hh] = Elt<DT>::f(row[hh]);
+        }
         float acc = 0.f;
-        for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(expf(Elt<DT>::f(row[hh]) - s_M[hh]) / s_L[hh]);
+        for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(__expf(lv[hh] - s_M[hh]) / s_L[hh]);
         L.votes[bh * g.S_cap + pos] += rnd<DT>(acc / (float)G);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -674,8 +695,16 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, 
         bool first = true;
         for (int t = lane; t < 64; t += 32) {
             const T* row = lg + ((size_t)bh * S_tot + g.S_cap + (size_t)slot * 64 + t) * G;
+            float lv[MM_G];
+            if (G == 4) {
+                const uint2 u = *reinterpret_cast<const uint2*>(row);
+                const T* tt = reinterpret_cast<const T*>(&u);
+                for (int hh = 0; hh < 4; ++hh) lv[hh] = Elt<DT>::f(tt[hh]);
+            } else {
+                for (int hh = 0; hh < G; ++hh) lv[hh] = Elt<DT>::f(row[hh]);
+            }
             float acc = 0.f;
-            for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(expf(Elt<DT>::f(row[hh]) - s_M[hh]) / s_L[hh]);
+            for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(__expf(lv[hh] - s_M[hh]) / s_L[hh]);
             const float mean = rnd<DT>(acc / (float)G);
             a = first ? mean : a + mean;
             first = false;

@@ -59,7 +59,7 @@ def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=Fal
     attn_t, cyc_t, step_t, tvals = [], [], [], []
     for _ in range(steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        torch.cuda._sleep(100000)
+        torch.cuda._sleep(2000000)
         ev[0].record()
         qr = st.append(q, kn, vn)
         ev[1].record()
