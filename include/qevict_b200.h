@@ -153,6 +153,22 @@ int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t
 int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
                         void* workspace, size_t workspace_bytes, qv_stream_t stream);
 
+/* qv_decode_attention without a workspace argument; no counterpart in the
+ * reference.  For callers that cannot allocate device memory between decode
+ * steps (a foreign-language host holding only the layer's pointers, or a
+ * serving loop that must not call cudaMalloc/cudaFree).  Its scratch is a
+ * fixed device array of QV_NOALLOC_SCRATCH_BYTES inside this library (8 MiB:
+ * batch 8 at the Llama-3-8B layer shape, 32 sticky + 32 Q windows of 64,
+ * local 512, fits); dims whose qv_decode_workspace_bytes exceeds it return
+ * QV_ESPACE with a message in qv_last_cuda_error().  The scratch is shared per
+ * device, so calls that overlap in time race on it; the first call on a
+ * device looks up the scratch address and should come before any capture or
+ * timed loop.  Results are those of qv_decode_attention, except that the
+ * logits are not exposed. */
+#define QV_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+int qv_decode_attention_noalloc(const qv_dims* d, const qv_layer* L, const void* q, void* out,
+                                qv_stream_t stream);
+
 /* One eviction cycle (every omega tokens): scoreboard, window competition,
  * segmented top-k, promotion, Q-cache rebuild (paths A/B/C) and slot moves.
  * Replaces EvictionManager.run_decode_cycle / update_local_history /

@@ -62,6 +62,7 @@ def lib():
         "qv_cycle_workspace_bytes": (sz, [D]),
         "qv_rope_append": (ctypes.c_int, [D, Lp, vp, vp, vp, vp, vp, vp, vp]),
         "qv_decode_attention": (ctypes.c_int, [D, Lp, vp, vp, vp, sz, vp]),
+        "qv_decode_attention_noalloc": (ctypes.c_int, [D, Lp, vp, vp, vp]),
         "qv_rope": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, i32, vp]),
         "qv_evict_cycle": (ctypes.c_int, [D, Lp, vp, sz, vp]),
         "qv_prefill_build": (ctypes.c_int, [D, Lp, vp, vp, i32, vp, i32, vp]),
@@ -86,7 +87,8 @@ def exported_symbols():
     """Names the header declares (used by the CPU test that checks the exports)."""
     return ["qv_ring_windows", "qv_main_capacity", "qv_decode_workspace_bytes", "qv_decode_path",
             "qv_decode_logits_offset",
-            "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention", "qv_evict_cycle",
+            "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention",
+            "qv_decode_attention_noalloc", "qv_evict_cycle",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_read_error",
             "qv_last_cuda_error", "qv_version"]

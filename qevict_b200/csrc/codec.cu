@@ -13,6 +13,11 @@ int set_cuda_error(cudaError_t e) {
     return QV_ECUDA;
 }
 
+int set_error_text(const char* msg) {
+    snprintf(g_cuda_err, sizeof(g_cuda_err), "%s", msg);
+    return QV_OK;
+}
+
 int check_launch() {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QV_OK : set_cuda_error(e);
