@@ -1,0 +1,55 @@
+"""The C-ABI library: it loads without a GPU and exports every function the header declares.
+
+Only host-side size helpers are called here (they touch no device).
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from qevict_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "qevict_b200.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(qv_[a-z0-9_]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_lists_the_entry_points():
+    names = header_functions()
+    for must in ("qv_decode_attention", "qv_evict_cycle", "qv_rope_append", "qv_prefill_build",
+                 "qv_prefill_attention", "qv_quantize_k", "qv_quantize_v", "qv_dequantize",
+                 "qv_decode_attention_noalloc"):
+        assert must in names
+    assert sorted(N.exported_symbols()) == names
+
+
+def test_library_exports_every_header_symbol():
+    lib = N.lib()
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert lib.qv_version().decode()
+
+
+@pytest.mark.parametrize("local,omega,kw,expect_R", [(512, 64, 32, 9), (128, 64, 3, 3), (256, 32, 0, 9)])
+def test_slot_layout_sizes(local, omega, kw, expect_R):
+    d = N.QvDims(1, 8, 4, 128, omega, 64, local, kw, 16, 512, 8, N.QV_BF16, 0)
+    assert N.lib().qv_ring_windows(ctypes.byref(d)) == expect_R
+    assert N.lib().qv_main_capacity(ctypes.byref(d)) == 64 + (kw + expect_R) * omega
+
+
+def test_invalid_dims_rejected():
+    bad = [N.QvDims(1, 8, 4, 96, 64, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0),   # head_dim 96
+           N.QvDims(1, 8, 4, 128, 64, 64, 500, 32, 32, 512, 8, N.QV_BF16, 0),  # local not whole windows
+           N.QvDims(1, 8, 4, 128, 64, 64, 512, 32, 32, 512, 3, N.QV_BF16, 0),  # 3-bit codes
+           N.QvDims(1, 8, 16, 128, 64, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0)]  # group 16
+    for d in bad:
+        assert N.lib().qv_ring_windows(ctypes.byref(d)) == -1
+        assert N.lib().qv_main_capacity(ctypes.byref(d)) == -1
