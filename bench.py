@@ -290,10 +290,12 @@ def run_ours(args):
     achieved = (sum(bytes_) / len(bytes_)) / avg_dur / 1e9
     peak, peak_kind = peaks()
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "decode_attention_traffic.json")
+    tf = os.path.join(ROOT, "profiles", "decode_attention_traffic.txt")
     if os.path.exists(tf):
         with open(tf) as f:
-            traffic = json.load(f).get("c2_bytes_per_launch")
+            for ln in f:
+                if ln.startswith("bytes_per_launch"):
+                    traffic = int(ln.split("=")[1])
 
     if rank == 0:
         line = {
