@@ -137,12 +137,216 @@ __device__ __forceinline__ float logit_round(float dot) {
     return rnd<DT>(div_sqrt128(rnd<DT>(dot)));
 }
 
+// Sum over the G heads of one token's probabilities, each rounded to the KV
+// dtype: sum_h rnd(exp(logit_h - M_h) / L_h).  row = the token's G rounded logits.
+template <int DT>
+__device__ __forceinline__ float bits_to_f(uint32_t b16);
+template <> __device__ __forceinline__ float bits_to_f<QV_BF16>(uint32_t b16) { return __uint_as_float(b16 << 16); }
+template <> __device__ __forceinline__ float bits_to_f<QV_F16>(uint32_t b16) {
+    return __half2float(__ushort_as_half((unsigned short)b16));
+}
+template <int DT>
+__device__ __forceinline__ float group_prob_sum(const typename Elt<DT>::T* row, int G, const float* sM, const float* sL) {
+    float acc = 0.f;
+    if (G == 4) {
+        const uint2 u = __ldcg(reinterpret_cast<const uint2*>(row));
+        acc += rnd<DT>(__expf(bits_to_f<DT>(u.x & 0xffffu) - sM[0]) / sL[0]);
+        acc += rnd<DT>(__expf(bits_to_f<DT>(u.x >> 16) - sM[1]) / sL[1]);
+        acc += rnd<DT>(__expf(bits_to_f<DT>(u.y & 0xffffu) - sM[2]) / sL[2]);
+        acc += rnd<DT>(__expf(bits_to_f<DT>(u.y >> 16) - sM[3]) / sL[3]);
+    } else {
+        for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(__expf(Elt<DT>::f(row[hh]) - sM[hh]) / sL[hh]);
+    }
+    return acc;
+}
+
+// Shared scratch of one combine unit, in floats: per-head partial maxima and
+// weights [G][2*64], per-head totals, the two output accumulators [2][G*128]
+// and one liveness code per 64-token block of the unit.
+constexpr int MM_CMB_MAXBLK = 1024;
+constexpr int MM_CMB_SMEM = 2 * MM_G * 128 + 2 * MM_G + 2 * MM_G * 128 + MM_CMB_MAXBLK / 4;
+
+// One combine unit: merge the per-CTA partials of one (sequence, KV head) bh,
+// write this unit's slice of its output, and fold the exact probabilities of
+// this unit's 64-token blocks into the vote ledger / Q-window scores.  Run by
+// nthr threads (tid < nthr, nthr a multiple of 32 and >= 32*G) that synchronise
+// with sync(); N0 is the token count the attention pass saw (new token
+// included).  Written for latency: every phase issues its global loads
+// together, so a unit costs a handful of dependent L2 round trips.
+template <int DT, typename Sync>
+__device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, void* __restrict__ out,
+                                             const float* __restrict__ partial, const void* __restrict__ logits,
+                                             const MmPlan& P, int N0, long long bh, int chunk, int nchunks,
+                                             int blocks_per_chunk, float* sm, int tid, int nthr, Sync sync) {
+    constexpr int MAXP = 64;
+    float(*s_m)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm);             // maxima, then weights
+    float(*s_l)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm + MM_G * 128);
+    float* s_M = sm + 2 * MM_G * 128;
+    float* s_L = s_M + MM_G;
+    float(*s_acc)[MM_G * 128] = reinterpret_cast<float(*)[MM_G * 128]>(s_L + MM_G);
+    unsigned char* s_live = reinterpret_cast<unsigned char*>(s_L + MM_G + 2 * MM_G * 128);
+    using T = typename Elt<DT>::T;
+    const int n_mblk = g.S_cap / 64;              // 64-token main blocks, then one per Q window
+    const int n_blk = n_mblk + g.qw;
+    const int b = (int)(bh / g.H), h = (int)(bh % g.H);
+    const int G = g.G;
+    const int cw = (N0 - g.sink) / g.om;
+    const int tv = (N0 - g.sink) % g.om + 1;
+    const size_t S_tot = (size_t)g.S_cap + (size_t)g.qw * g.om;
+    int f0, c0, f1, c1;
+    mm_zone_ctas(P, bh, 0, &f0, &c0);
+    mm_zone_ctas(P, bh, 1, &f1, &c1);
+    const int np = c0 + c1;
+    const float* pz0 = partial + ((size_t)bh * 2 + 0) * P.pmax * G * 130;
+    const float* pz1 = partial + ((size_t)bh * 2 + 1) * P.pmax * G * 130;
+    auto prow = [&](int s) { return s < c0 ? pz0 + (size_t)s * G * 130 : pz1 + (size_t)(s - c0) * G * 130; };
+    const int blk0 = chunk * blocks_per_chunk;
+    const int blk1 = min(blk0 + blocks_per_chunk, n_blk);
+    // (A) partial maxima / sums, and a liveness code per block of this unit:
+    //     0 = no live token, 1 = all live, 2 = live below offset tv (current window)
+    for (int t = tid; t < G * np; t += nthr) {
+        const int hh = t / np, s = t % np;
+        const float* pr = prow(s) + hh * 130;
+        s_m[hh][s] = __ldcg(pr);
+        s_l[hh][s] = __ldcg(pr + 1);
+    }
+    {
+        const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
+        for (int blk = blk0 + tid; blk < blk1; blk += nthr) {
+            unsigned char code;
+            if (blk < sink_blk) code = 1;
+            else if (blk < ring_blk) code = L.sticky_wid[bh * g.kw + (blk - sink_blk)] >= 0;
+            else if (blk < n_mblk) {
+                const int pos = blk * 64;
+                code = mm_item_live(g, pos + 63, cw, 0) ? 1 : 2;
+            } else code = L.q_wid[bh * g.qw + (blk - n_mblk)] >= 0;
+            s_live[blk - blk0] = code;
+        }
+    }
+    sync();
+    // (B) one warp per head: total maximum, normaliser and per-partial weights
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        if (warp < G) {
+            const int hh = warp;
+            float M = -INFINITY;
+            for (int s = lane; s < np; s += 32) M = fmaxf(M, s_m[hh][s]);
+            M = warp_max(M);
+            float Ls = 0.f;
+            for (int s = lane; s < np; s += 32) {
+                const float ms = s_m[hh][s];
+                const float w = ms > -INFINITY ? __expf(ms - M) : 0.f;
+                Ls += s_l[hh][s] * w;
+                s_m[hh][s] = w;
+            }
+            Ls = warp_sum(Ls);
+            if (lane == 0) { s_M[hh] = M; s_L[hh] = Ls; }
+        }
+    }
+    // (C) this unit's slice of the G*128 output elements; (element, partial)
+    //     products are spread over all threads and reduced in shared memory
+    const int ne = G * 128;
+    const int per = (ne + nchunks - 1) / nchunks;
+    const int e0 = min(chunk * per, ne), e1 = min(e0 + per, ne);
+    for (int t = tid; t < 2 * (e1 - e0); t += nthr) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
+    sync();
+    {
+        const int work = (e1 - e0) * np;
+        for (int t = tid; t < work; t += nthr) {
+            const int el = e0 + t / np, s = t % np;
+            const int hh = el >> 7, d = el & 127;
+            atomicAdd(&s_acc[s < c0 ? 0 : 1][el], __ldcg(prow(s) + hh * 130 + 2 + d) * s_m[hh][s]);
+        }
+    }
+    sync();
+    {
+        const bool has_q = L.seq[b * 4 + 1] > 0;
+        for (int el = e0 + tid; el < e1; el += nthr) {
+            const int hh = el >> 7, d = el & 127;
+            const float inv = 1.f / s_L[hh];
+            const float om_ = s_acc[0][el], oq = s_acc[1][el];
+            const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
+            st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
+        }
+    }
+    // (D) main-zone tokens of this unit, four per thread per round with all
+    //     loads issued before any ledger store
+    const T* lg = reinterpret_cast<const T*>(logits) + (size_t)bh * S_tot * G;
+    float* votes = L.votes + bh * g.S_cap;
+    const int p_beg = blk0 * 64, p_end = min(blk1, n_mblk) * 64;
+    for (int base = p_beg + tid; base < p_end; base += 4 * nthr) {
+        bool lv[4];
+        float vo[4], acc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int pos = base + u * nthr;
+            lv[u] = false;
+            if (pos < p_end) {
+                const int code = s_live[(pos >> 6) - blk0];
+                lv[u] = code == 1 || (code == 2 && (pos & 63) < tv);
+            }
+            if (lv[u]) {
+                acc[u] = group_prob_sum<DT>(lg + (size_t)pos * G, G, s_M, s_L);
+                vo[u] = votes[pos];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (lv[u]) votes[base + u * nthr] = vo[u] + rnd<DT>(acc[u] / (float)G);
+    }
+    // (E) Q windows of this unit: one warp per window, two tokens per lane
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int blk = max(blk0, n_mblk) + warp; blk < blk1; blk += nthr >> 5) {
+            if (!s_live[blk - blk0]) continue;
+            const int slot = blk - n_mblk;
+            const T* wl = lg + ((size_t)g.S_cap + (size_t)slot * 64) * G;
+            const float a0 = group_prob_sum<DT>(wl + (size_t)lane * G, G, s_M, s_L);
+            const float a1 = group_prob_sum<DT>(wl + (size_t)(lane + 32) * G, G, s_M, s_L);
+            float a = rnd<DT>(a0 / (float)G) + rnd<DT>(a1 / (float)G);
+            a = warp_sum(a);
+            if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
+        }
+    }
+    sync();   // the scratch is reused by the next unit
+}
+
+struct BlockSync {
+    __device__ void operator()() const { __syncthreads(); }
+};
+struct ConsumerSync {
+    __device__ void operator()() const { consumer_sync(); }
+};
+
+// Barrier across all CTAs of a grid whose CTAs are all resident (cooperative
+// launch).  Called by one thread per CTA; count must be zero before the first
+// arrival (the last arrival resets it), gen may hold any value.  Gives up after
+// about two seconds and returns false.
+__device__ __forceinline__ bool grid_barrier(int* count, int* gen, int n) {
+    volatile int* vgen = gen;
+    const int g0 = *vgen;
+    __threadfence();
+    if (atomicAdd(count, 1) == n - 1) {
+        *count = 0;
+        __threadfence();
+        atomicAdd(gen, 1);
+        return true;
+    }
+    const uint64_t t0 = global_ns();
+    while (*vgen == g0) {
+        if (global_ns() - t0 > 2000000000ull) return false;
+        __nanosleep(64);
+    }
+    __threadfence();
+    return true;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(MM_THREADS, 1)
 decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ CUtensorMap tmKQ, const __grid_constant__ CUtensorMap tmVQ,
                   Geo g, qv_layer L, const void* __restrict__ q, int* tickets, float* partial,
-                  void* logits, MmPlan P) {
+                  void* logits, MmPlan P, void* __restrict__ out, int fuse_chunks, int blocks_per_chunk) {
     using T = typename Elt<DT>::T;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -178,11 +382,15 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     auto skipped = [&](long long i) -> bool {
         return i - i0 < MM_SKIPMAP ? s_skip[i - i0] != 0 : mm_skip(g, L, P, i / P.ipb, (int)(i % P.ipb));
     };
-    // wait for the preceding kernel (RoPE + append) before touching q or the cache
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The preceding kernel (RoPE + append) writes q and one new token per
+    // (sequence, KV head), at token index N0 of the ring; the token counter, the
+    // slot tables and every other cached token are final before it starts.  So
+    // the producer streams all other items before waiting for it, and only the
+    // item holding the new token, and the consumers' read of q, wait.
     const int N0 = L.step[0];
     const int cw = (N0 - g.sink) / g.om;
     const int tv = (N0 - g.sink) % g.om + 1;
+    const int j_new = (g.ring_base() + (cw % g.R) * 64 + tv - 1) / MM_MT;
 
     // --------------------------------------------------------------- producer
     if (warp == MM_CW) {
@@ -191,6 +399,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             prefetch_tensormap(&tmV);
             prefetch_tensormap(&tmKQ);
             prefetch_tensormap(&tmVQ);
+            bool waited = false;
             int k = 0;
             long long bh = i0 / P.ipb;
             int j = (int)(i0 % P.ipb) - 1;
@@ -198,6 +407,10 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             for (long long i = i0; i < i1; ++i) {
                 if (++j == P.ipb) { j = 0; ++bh; }
                 if (skipped(i)) continue;
+                if (j == j_new && !waited) {
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    waited = true;
+                }
                 const int s = k % NS;
                 if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
                     set_err(L.err, QV_DERR_LAYOUT);
@@ -247,6 +460,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         ls[0] = ls[1] = spp[0] = spp[1] = svz[0] = svz[1] = 0.f;
     };
 
+    // q is written by the preceding kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     auto load_q = [&](long long bh) {
         const int b = (int)(bh / g.H), h = (int)(bh % g.H);
         consumer_sync();
@@ -388,28 +603,43 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const unsigned char* stp = stages + s * MM_STAGE;
         if (zone == 0) {
             // ---------------- main zone: 32 tokens = 2 m-tiles -----------------
-            float sc[2][4];
+            // two accumulators per m-tile (d < 64 and d >= 64) halve the chain
+            // of dependent MMAs
+            float sc[2][4], sc2[2][4];
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) sc[mt][r] = 0.f;
+                for (int r = 0; r < 4; ++r) sc[mt][r] = sc2[mt][r] = 0.f;
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
+            for (int kk = 0; kk < 4; ++kk) {
                 const int d = 16 * kk + 8 * (mi >> 1);
 #pragma unroll
                 for (int mt = 0; mt < 2; ++mt) {
                     const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
-                    uint32_t a[4];
-                    ldsm_x4(st + (d >= 64 ? 4096 : 0) + swz(row, (d & 63) >> 3), a[0], a[1], a[2], a[3]);
+                    uint32_t a[4], a2[4];
+                    ldsm_x4(st + swz(row, d >> 3), a[0], a[1], a[2], a[3]);
+                    ldsm_x4(st + 4096 + swz(row, d >> 3), a2[0], a2[1], a2[2], a2[3]);
                     mma_kv<DT>(sc[mt], a, bq[kk]);
+                    mma_kv<DT>(sc2[mt], a2, bq[kk + 4]);
                 }
             }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) sc[mt][r] += sc2[mt][r];
             float lg[2][4];   // per column: [mt*2 + rowhalf]
             const int pos0 = MM_MT * j;
+            // token t of this item is live iff off0 + t < lim: only the current
+            // ring window has an unwritten tail
+            int off0 = 0, lim = 64;
+            if (pos0 >= g.ring_base()) {
+                off0 = (pos0 - g.ring_base()) & 63;
+                if (!mm_item_live(g, pos0 + 63 - off0, cw, 0)) lim = tv;
+            }
 #pragma unroll
             for (int mt = 0; mt < 2; ++mt) {
                 const int tA = 16 * mt + gq, tB = tA + 8;
-                const bool la = mm_item_live(g, pos0 + tA, cw, tv), lb = mm_item_live(g, pos0 + tB, cw, tv);
+                const bool la = off0 + tA < lim, lb = off0 + tB < lim;
                 const float v0 = la ? logit_round<DT>(sc[mt][0]) : -INFINITY;
                 const float v1 = la ? logit_round<DT>(sc[mt][1]) : -INFINITY;
                 const float v2 = lb ? logit_round<DT>(sc[mt][2]) : -INFINITY;
@@ -563,6 +793,28 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (fuse_chunks > 0) {
+        // Combine in this grid (small batches): every CTA is resident, so after
+        // a grid-wide barrier all partials and logits are visible and the
+        // (b, h, chunk) units are spread over the CTAs.
+        __shared__ int s_pass;
+        __threadfence();
+        consumer_sync();
+        if (threadIdx.x == 0) {
+            s_pass = grid_barrier(tickets + 1, tickets + 2, (int)gridDim.x) ? 1 : 0;
+            if (!s_pass) set_err(L.err, QV_DERR_LAYOUT);
+            // every CTA read the token counter before arriving
+            else if (c == 0) L.step[0] = N0 + 1;
+        }
+        consumer_sync();
+        if (!s_pass) return;
+        float* sm = reinterpret_cast<float*>(stages);
+        const int units = fuse_chunks * g.B * g.H;
+        for (int u = c; u < units; u += (int)gridDim.x)
+            combine_unit<DT>(g, L, out, partial, logits, P, N0, u / fuse_chunks, u % fuse_chunks, fuse_chunks,
+                             blocks_per_chunk, sm, (int)threadIdx.x, MM_CW * 32, ConsumerSync{});
+        return;
+    }
     // let the combine grid get scheduled while this grid drains (it waits for
     // this grid's completion before reading anything)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -578,140 +830,20 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     }
 }
 
-// Merge the per-CTA partials of one (sequence, KV head), write the output, and
-// fold the exact probabilities of a chunk of its tokens into the vote ledger /
-// Q-window scores.  grid = (chunks, B*H); chunk 0 also writes the output.
+// Separate combine kernel (used when the batch is large enough that a
+// dedicated grid of many small blocks beats the attention kernel's own CTAs).
+// grid = (chunks, B*H); chunk 0..chunks-1 of each (b, h).
 template <int DT>
 __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, void* __restrict__ out,
                                                              const float* __restrict__ partial,
                                                              const void* __restrict__ logits, MmPlan P,
                                                              int blocks_per_chunk) {
-    // 64-token blocks of this (b, h): main zone blocks, then one per Q window
-    const int n_mblk = g.S_cap / 64;
-    const int n_blk = n_mblk + g.qw;
+    __shared__ float sm[MM_CMB_SMEM];
     // wait for the streaming kernel (programmatic dependent launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    constexpr int MAXP = 64;
-    __shared__ float s_m[MM_G][2 * MAXP];
-    __shared__ float s_w[MM_G][2 * MAXP];
-    __shared__ float s_l[MM_G][2 * MAXP];
-    __shared__ float s_M[MM_G], s_L[MM_G];
-    const long long bh = blockIdx.y;
-    const int b = (int)(bh / g.H), h = (int)(bh % g.H);
-    const int G = g.G;
     const int N0 = L.step[0] - 1;
-    const int cw = (N0 - g.sink) / g.om;
-    const int tv = (N0 - g.sink) % g.om + 1;
-    const size_t S_tot = (size_t)g.S_cap + (size_t)g.qw * g.om;
-    int f0, c0, f1, c1;
-    mm_zone_ctas(P, bh, 0, &f0, &c0);
-    mm_zone_ctas(P, bh, 1, &f1, &c1);
-    const int np = c0 + c1;
-    const float* pz[2] = {partial + ((size_t)bh * 2 + 0) * P.pmax * G * 130,
-                          partial + ((size_t)bh * 2 + 1) * P.pmax * G * 130};
-    for (int t = threadIdx.x; t < G * np; t += blockDim.x) {
-        const int hh = t / np, s = t % np;
-        const float* pr = s < c0 ? pz[0] + (size_t)s * G * 130 + hh * 130 : pz[1] + (size_t)(s - c0) * G * 130 + hh * 130;
-        s_m[hh][s] = pr[0];
-        s_l[hh][s] = pr[1];
-    }
-    __syncthreads();
-    if (threadIdx.x < G) {
-        const int hh = threadIdx.x;
-        float M = -INFINITY;
-        for (int s = 0; s < np; ++s) M = fmaxf(M, s_m[hh][s]);
-        float Ls = 0.f;
-        for (int s = 0; s < np; ++s)
-            if (s_m[hh][s] > -INFINITY) Ls += s_l[hh][s] * __expf(s_m[hh][s] - M);
-        s_M[hh] = M;
-        s_L[hh] = Ls;
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < G * np; t += blockDim.x) {
-        const int hh = t / np, s = t % np;
-        s_w[hh][s] = s_m[hh][s] > -INFINITY ? __expf(s_m[hh][s] - s_M[hh]) : 0.f;
-    }
-    __syncthreads();
-    // this CTA's slice of the G*128 output elements; (element, partial) products
-    // are spread over all threads and reduced in shared memory
-    {
-        __shared__ float s_acc[2][MM_G * 128];
-        const int ne = G * 128;
-        const int per = (ne + gridDim.x - 1) / gridDim.x;
-        const int e0 = blockIdx.x * per, e1 = min(e0 + per, ne);
-        for (int t = threadIdx.x; t < 2 * (e1 - e0); t += blockDim.x) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
-        __syncthreads();
-        const int work = (e1 - e0) * np;
-        for (int t = threadIdx.x; t < work; t += blockDim.x) {
-            const int el = e0 + t / np, s = t % np;
-            const int hh = el >> 7, d = el & 127;
-            const float* pr = s < c0 ? pz[0] + (size_t)s * G * 130 : pz[1] + (size_t)(s - c0) * G * 130;
-            atomicAdd(&s_acc[s < c0 ? 0 : 1][el], pr[hh * 130 + 2 + d] * s_w[hh][s]);
-        }
-        __syncthreads();
-        const bool has_q = L.seq[b * 4 + 1] > 0;
-        for (int el = e0 + threadIdx.x; el < e1; el += blockDim.x) {
-            const int hh = el >> 7, d = el & 127;
-            const float inv = 1.f / s_L[hh];
-            const float om_ = s_acc[0][el], oq = s_acc[1][el];
-            const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
-            st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
-        }
-    }
-    // this chunk's 64-token blocks: main tiles first, then Q windows
-    const int blk0 = blockIdx.x * blocks_per_chunk;
-    const int blk1 = min(blk0 + blocks_per_chunk, n_blk);
-    const int32_t* swid = L.sticky_wid + bh * g.kw;
-    const int32_t* qwid = L.q_wid + bh * g.qw;
-    using T = typename Elt<DT>::T;
-    const T* lg = reinterpret_cast<const T*>(logits);
-    const int main_end = min(blk1, n_mblk) * 64;
-    const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
-    for (int pos = blk0 * 64 + threadIdx.x; pos < main_end; pos += blockDim.x) {
-        const int blk = pos >> 6;
-        bool live;
-        if (blk < sink_blk) live = true;
-        else if (blk < ring_blk) live = swid[blk - sink_blk] >= 0;
-        else live = mm_live(g, swid, pos, cw, tv);
-        if (!live) continue;
-        const T* row = lg + ((size_t)bh * S_tot + pos) * G;
-        float lv[MM_G];
-        if (G == 4) {
-            const uint2 u = *reinterpret_cast<const uint2*>(row);
-            const T* t = reinterpret_cast<const T*>(&u);
-            for (int hh = 0; hh < 4; ++hh) lv[hh] = Elt<DT>::f(t[hh]);
-        } else {
-            for (int hh = 0; hh < G; ++hh) lv[hh] = Elt<DT>::f(row[hh]);
-        }
-        float acc = 0.f;
-        for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(__expf(lv[hh] - s_M[hh]) / s_L[hh]);
-        L.votes[bh * g.S_cap + pos] += rnd<DT>(acc / (float)G);
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int blk = max(blk0, n_mblk) + warp; blk < blk1; blk += blockDim.x >> 5) {
-        const int slot = blk - n_mblk;
-        if (qwid[slot] < 0) continue;
-        float a = 0.f;
-        bool first = true;
-        for (int t = lane; t < 64; t += 32) {
-            const T* row = lg + ((size_t)bh * S_tot + g.S_cap + (size_t)slot * 64 + t) * G;
-            float lv[MM_G];
-            if (G == 4) {
-                const uint2 u = *reinterpret_cast<const uint2*>(row);
-                const T* tt = reinterpret_cast<const T*>(&u);
-                for (int hh = 0; hh < 4; ++hh) lv[hh] = Elt<DT>::f(tt[hh]);
-            } else {
-                for (int hh = 0; hh < G; ++hh) lv[hh] = Elt<DT>::f(row[hh]);
-            }
-            float acc = 0.f;
-            for (int hh = 0; hh < G; ++hh) acc += rnd<DT>(__expf(lv[hh] - s_M[hh]) / s_L[hh]);
-            const float mean = rnd<DT>(acc / (float)G);
-            a = first ? mean : a + mean;
-            first = false;
-        }
-        a = warp_sum(a);
-        if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
-    }
+    combine_unit<DT>(g, L, out, partial, logits, P, N0, blockIdx.y, blockIdx.x, gridDim.x, blocks_per_chunk, sm,
+                     threadIdx.x, blockDim.x, BlockSync{});
 }
 
 // ------------------------------------------------------------------ host side
@@ -789,7 +921,8 @@ size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
 
 int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s) {
     MmPlan P = mm_plan(g);
-    if (P.pmax > 64 || P.ns < 2) return QV_EINVAL;
+    // a consumer warp may wait on a stage only one fill ahead of it: stages >= warps
+    if (P.pmax > 64 || P.ns < MM_CW) return QV_EINVAL;
     size_t op, ol;
     mm_ws_bytes(g, &op, &ol);
     char* base = reinterpret_cast<char*>(ws);
@@ -810,39 +943,41 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     void* lgt = base + ol;
     const int BH = g.B * g.H;
     const int n_blk = g.S_cap / 64 + g.qw;
-    int chunks = (2 * sm_count() + BH - 1) / BH;
+    // Small batches combine inside the attention grid after a grid-wide barrier
+    // (one launch, no second-kernel tail); large ones use a separate grid of
+    // many small blocks, chained with programmatic dependent launch.
+    const bool fuse = BH <= P.nC;
+    int chunks = fuse ? P.nC / BH : (2 * sm_count() + BH - 1) / BH;
     if (chunks > n_blk) chunks = n_blk;
+    if (chunks < (n_blk + MM_CMB_MAXBLK - 1) / MM_CMB_MAXBLK) chunks = (n_blk + MM_CMB_MAXBLK - 1) / MM_CMB_MAXBLK;
     if (chunks < 1) chunks = 1;
     const int bpc = (n_blk + chunks - 1) / chunks;
     chunks = (n_blk + bpc - 1) / bpc;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
     cudaLaunchConfig_t cfg1 = {};
     cfg1.gridDim = dim3(P.nC);
     cfg1.blockDim = dim3(MM_THREADS);
     cfg1.dynamicSmemBytes = smem;
     cfg1.stream = s;
     cfg1.attrs = attr;
-    cfg1.numAttrs = 1;
+    cfg1.numAttrs = fuse ? 2 : 1;
     cudaLaunchConfig_t cfg2 = cfg1;
     cfg2.gridDim = dim3(chunks, BH);
     cfg2.blockDim = dim3(256);
     cfg2.dynamicSmemBytes = 0;
-    cudaError_t e;
-    if (g.dt == QV_BF16) {
-        e = ensure_smem(decode_mma_kernel<QV_BF16>, smem, &cached[1]);
-        if (e != cudaSuccess) return set_cuda_error(e);
-        e = cudaLaunchKernelEx(&cfg1, decode_mma_kernel<QV_BF16>, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
-        if (e != cudaSuccess) return set_cuda_error(e);
-        e = cudaLaunchKernelEx(&cfg2, decode_combine_kernel<QV_BF16>, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
-    } else {
-        e = ensure_smem(decode_mma_kernel<QV_F16>, smem, &cached[2]);
-        if (e != cudaSuccess) return set_cuda_error(e);
-        e = cudaLaunchKernelEx(&cfg1, decode_mma_kernel<QV_F16>, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
-        if (e != cudaSuccess) return set_cuda_error(e);
-        e = cudaLaunchKernelEx(&cfg2, decode_combine_kernel<QV_F16>, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
-    }
+    cfg2.numAttrs = 1;
+    const int fchunks = fuse ? chunks : 0;
+    auto kern = g.dt == QV_BF16 ? decode_mma_kernel<QV_BF16> : decode_mma_kernel<QV_F16>;
+    auto comb = g.dt == QV_BF16 ? decode_combine_kernel<QV_BF16> : decode_combine_kernel<QV_F16>;
+    cudaError_t e = ensure_smem(kern, smem, &cached[g.dt == QV_BF16 ? 1 : 2]);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P, out, fchunks, bpc);
+    if (e != cudaSuccess) return set_cuda_error(e);
+    if (!fuse) e = cudaLaunchKernelEx(&cfg2, comb, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
     if (e != cudaSuccess) return set_cuda_error(e);
     return check_launch();
 }

@@ -299,6 +299,32 @@ def gen_prefill():
     save("prefill", **out)
 
 
+# ---------------------------------------------------------------------------
+# 6. budget allocator over a grid of prompt lengths and ratios
+# ---------------------------------------------------------------------------
+def gen_budget():
+    import contextlib
+    import io
+    from src.models.kv_cache.allocator import compute_budget as ref_budget
+    rows, outs = [], []
+    for new_tokens in (100, 1000, 4096, 32768, 131072):
+        for r in (5, 20, 50, 100):
+            for fixed, local in ((True, 512), (True, 256), (False, 0)):
+                for q_ratio in (0, 10, 50):
+                    for bits in (8, 4):
+                        for omega in (16, 64):
+                            args = dict(total_cache_ratio=r, sink_tokens=64, use_fixed_local_tokens=fixed,
+                                        local_num_tokens=local, local_cache_ratio=50, q_ratio=q_ratio,
+                                        quant_bit_width=bits, head_dim=128, omega=omega,
+                                        new_tokens=new_tokens, max_tokens=512, layer_idx=1)
+                            with contextlib.redirect_stdout(io.StringIO()):
+                                res = ref_budget(**args)
+                            rows.append([new_tokens, r, int(fixed), local, q_ratio, bits, omega])
+                            outs.append([res.local_num, res.k_windows, res.q_windows_count, res.q_num,
+                                         res.quant_bytes_len])
+    save("budget", inputs=np.array(rows, np.int64), outputs=np.array(outs, np.int64))
+
+
 if __name__ == "__main__":
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     gen_codec()
@@ -309,3 +335,4 @@ if __name__ == "__main__":
     gen_module("module_fp32", "fp32", seed=21)
     gen_module("module_bf16", "bf16", seed=22)
     gen_prefill()
+    gen_budget()
