@@ -54,6 +54,9 @@ struct MmPlan {
 };
 
 __host__ __device__ inline int mm_cta_of(const MmPlan& P, long long i) {
+    // 32-bit division whenever the product fits (every practical size)
+    if ((unsigned long long)P.total * (unsigned)P.nC < (1ull << 32))
+        return (int)((unsigned)i * (unsigned)P.nC / (unsigned)P.total);
     return (int)(i * P.nC / P.total);
 }
 __host__ __device__ inline long long mm_first_item(const MmPlan& P, int c) {
@@ -160,6 +163,16 @@ __device__ __forceinline__ float group_prob_sum(const typename Elt<DT>::T* row, 
     return acc;
 }
 
+// The same for G = 4 from the token's four logits already loaded as a uint2.
+template <int DT>
+__device__ __forceinline__ float group_prob_sum4(uint2 u, const float* sM, const float* sL) {
+    float acc = rnd<DT>(__expf(bits_to_f<DT>(u.x & 0xffffu) - sM[0]) / sL[0]);
+    acc += rnd<DT>(__expf(bits_to_f<DT>(u.x >> 16) - sM[1]) / sL[1]);
+    acc += rnd<DT>(__expf(bits_to_f<DT>(u.y & 0xffffu) - sM[2]) / sL[2]);
+    acc += rnd<DT>(__expf(bits_to_f<DT>(u.y >> 16) - sM[3]) / sL[3]);
+    return acc;
+}
+
 // Shared scratch of one combine unit, in floats: per-head partial maxima and
 // weights [G][2*64], per-head totals, the two output accumulators [2][G*128]
 // and one liveness code per 64-token block of the unit.
@@ -171,14 +184,17 @@ constexpr int MM_CMB_SMEM = 2 * MM_G * 128 + 2 * MM_G + 2 * MM_G * 128 + MM_CMB_
 // this unit's 64-token blocks into the vote ledger / Q-window scores.  Run by
 // nthr threads (tid < nthr, nthr a multiple of 32 and >= 32*G) that synchronise
 // with sync(); N0 is the token count the attention pass saw (new token
-// included).  Written for latency: every phase issues its global loads
-// together, so a unit costs a handful of dependent L2 round trips.
+// included).  Written for latency: a thread issues all global loads of its
+// first round of work (partial maxima, partial outputs, logits, ledger
+// entries) together before using any, so a unit costs about one dependent
+// L2 round trip plus the stores; larger units repeat rounds of four.
 template <int DT, typename Sync>
 __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, void* __restrict__ out,
                                              const float* __restrict__ partial, const void* __restrict__ logits,
                                              const MmPlan& P, int N0, long long bh, int chunk, int nchunks,
                                              int blocks_per_chunk, float* sm, int tid, int nthr, Sync sync) {
     constexpr int MAXP = 64;
+    constexpr int RW = 4;   // work items per thread per round
     float(*s_m)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm);             // maxima, then weights
     float(*s_l)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm + MM_G * 128);
     float* s_M = sm + 2 * MM_G * 128;
@@ -202,63 +218,151 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
     auto prow = [&](int s) { return s < c0 ? pz0 + (size_t)s * G * 130 : pz1 + (size_t)(s - c0) * G * 130; };
     const int blk0 = chunk * blocks_per_chunk;
     const int blk1 = min(blk0 + blocks_per_chunk, n_blk);
-    // (A) partial maxima / sums, and a liveness code per block of this unit:
-    //     0 = no live token, 1 = all live, 2 = live below offset tv (current window)
-    for (int t = tid; t < G * np; t += nthr) {
-        const int hh = t / np, s = t % np;
-        const float* pr = prow(s) + hh * 130;
-        s_m[hh][s] = __ldcg(pr);
-        s_l[hh][s] = __ldcg(pr + 1);
-    }
-    {
-        const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
-        for (int blk = blk0 + tid; blk < blk1; blk += nthr) {
-            unsigned char code;
-            if (blk < sink_blk) code = 1;
-            else if (blk < ring_blk) code = L.sticky_wid[bh * g.kw + (blk - sink_blk)] >= 0;
-            else if (blk < n_mblk) {
-                const int pos = blk * 64;
-                code = mm_item_live(g, pos + 63, cw, 0) ? 1 : 2;
-            } else code = L.q_wid[bh * g.qw + (blk - n_mblk)] >= 0;
-            s_live[blk - blk0] = code;
-        }
-    }
-    sync();
-    // (B) one warp per head: total maximum, normaliser and per-partial weights
-    {
-        const int warp = tid >> 5, lane = tid & 31;
-        if (warp < G) {
-            const int hh = warp;
-            float M = -INFINITY;
-            for (int s = lane; s < np; s += 32) M = fmaxf(M, s_m[hh][s]);
-            M = warp_max(M);
-            float Ls = 0.f;
-            for (int s = lane; s < np; s += 32) {
-                const float ms = s_m[hh][s];
-                const float w = ms > -INFINITY ? __expf(ms - M) : 0.f;
-                Ls += s_l[hh][s] * w;
-                s_m[hh][s] = w;
-            }
-            Ls = warp_sum(Ls);
-            if (lane == 0) { s_M[hh] = M; s_L[hh] = Ls; }
-        }
-    }
-    // (C) this unit's slice of the G*128 output elements; (element, partial)
-    //     products are spread over all threads and reduced in shared memory
     const int ne = G * 128;
     const int per = (ne + nchunks - 1) / nchunks;
     const int e0 = min(chunk * per, ne), e1 = min(e0 + per, ne);
-    for (int t = tid; t < 2 * (e1 - e0); t += nthr) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
-    sync();
-    {
-        const int work = (e1 - e0) * np;
-        for (int t = tid; t < work; t += nthr) {
-            const int el = e0 + t / np, s = t % np;
-            const int hh = el >> 7, d = el & 127;
-            atomicAdd(&s_acc[s < c0 ? 0 : 1][el], __ldcg(prow(s) + hh * 130 + 2 + d) * s_m[hh][s]);
+    const int ne_u = max(e1 - e0, 1);
+    const int work = (e1 - e0) * np;                  // (output element, partial) products, element fastest
+    const int p_beg = blk0 * 64, p_end = min(blk1, n_mblk) * 64;
+    const T* lg = reinterpret_cast<const T*>(logits) + (size_t)bh * S_tot * G;
+    float* votes = L.votes + bh * g.S_cap;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int q_blk = max(blk0, n_mblk) + warp;       // this warp's first Q window block
+
+    // ---- (A) issue every first-round load
+    float pm = -INFINITY, pl = 0.f;
+    const int am = tid < G * np ? tid : -1;
+    if (am >= 0) {
+        const float* pr = prow(am % np) + (am / np) * 130;
+        pm = __ldcg(pr);
+        pl = __ldcg(pr + 1);
+    }
+    int32_t live_src = 1;
+    const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
+    const int lb = blk0 + tid;
+    if (lb < blk1) {
+        if (lb >= sink_blk && lb < ring_blk) live_src = __ldcg(L.sticky_wid + bh * g.kw + (lb - sink_blk));
+        else if (lb >= n_mblk) live_src = __ldcg(L.q_wid + bh * g.qw + (lb - n_mblk));
+    }
+    float cv[RW];
+#pragma unroll
+    for (int u = 0; u < RW; ++u) {
+        const int t = tid + u * nthr;
+        cv[u] = 0.f;
+        if (t < work) cv[u] = __ldcg(prow(t / ne_u) + ((e0 + t % ne_u) >> 7) * 130 + 2 + ((e0 + t % ne_u) & 127));
+    }
+    uint2 dl[RW];
+    float dv[RW];
+#pragma unroll
+    for (int u = 0; u < RW; ++u) {
+        const int pos = p_beg + tid + u * nthr;
+        if (pos < p_end) {
+            dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
+            dv[u] = votes[pos];
         }
     }
+    uint2 el2[2] = {make_uint2(0, 0), make_uint2(0, 0)};
+    if (G == 4 && q_blk < blk1) {
+        const T* wl = lg + ((size_t)g.S_cap + (size_t)(q_blk - n_mblk) * 64) * G;
+        el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
+        el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
+    }
+    // ---- first uses: partial maxima / sums and the block liveness codes
+    //      (0 = no live token, 1 = all live, 2 = live below offset tv)
+    if (am >= 0) {
+        s_m[am / np][am % np] = pm;
+        s_l[am / np][am % np] = pl;
+    }
+    for (int blk = lb; blk < blk1; blk += nthr) {
+        if (blk != lb) {   // units with more blocks than threads
+            live_src = 1;
+            if (blk >= sink_blk && blk < ring_blk) live_src = L.sticky_wid[bh * g.kw + (blk - sink_blk)];
+            else if (blk >= n_mblk) live_src = L.q_wid[bh * g.qw + (blk - n_mblk)];
+        }
+        unsigned char code;
+        if (blk < sink_blk) code = 1;
+        else if (blk < ring_blk || blk >= n_mblk) code = live_src >= 0;
+        else code = mm_item_live(g, blk * 64 + 63, cw, 0) ? 1 : 2;
+        s_live[blk - blk0] = code;
+    }
+    for (int t = tid; t < 2 * (e1 - e0); t += nthr) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
     sync();
+    // ---- (B) one warp per head: total maximum, normaliser, per-partial weights
+    if (warp < G) {
+        const int hh = warp;
+        float M = -INFINITY;
+        for (int s2 = lane; s2 < np; s2 += 32) M = fmaxf(M, s_m[hh][s2]);
+        M = warp_max(M);
+        float Ls = 0.f;
+        for (int s2 = lane; s2 < np; s2 += 32) {
+            const float ms = s_m[hh][s2];
+            const float w = ms > -INFINITY ? __expf(ms - M) : 0.f;
+            Ls += s_l[hh][s2] * w;
+            s_m[hh][s2] = w;
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) { s_M[hh] = M; s_L[hh] = Ls; }
+    }
+    sync();
+    // ---- (C) output products, reduced in shared memory
+    for (int base = tid; base < work; base += RW * nthr) {
+#pragma unroll
+        for (int u = 0; u < RW; ++u) {
+            const int t = base + u * nthr;
+            if (base != tid && t < work)
+                cv[u] = __ldcg(prow(t / ne_u) + ((e0 + t % ne_u) >> 7) * 130 + 2 + ((e0 + t % ne_u) & 127));
+        }
+#pragma unroll
+        for (int u = 0; u < RW; ++u) {
+            const int t = base + u * nthr;
+            if (t < work) {
+                const int el = e0 + t % ne_u, s2 = t / ne_u;
+                atomicAdd(&s_acc[s2 < c0 ? 0 : 1][el], cv[u] * s_m[el >> 7][s2]);
+            }
+        }
+    }
+    // ---- (D) main-zone tokens: exact probabilities into the vote ledger
+    for (int base = p_beg + tid; base < p_end; base += RW * nthr) {
+        if (base != p_beg + tid) {
+#pragma unroll
+            for (int u = 0; u < RW; ++u) {
+                const int pos = base + u * nthr;
+                if (pos < p_end) {
+                    dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
+                    dv[u] = votes[pos];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < RW; ++u) {
+            const int pos = base + u * nthr;
+            if (pos >= p_end) continue;
+            const int code = s_live[(pos >> 6) - blk0];
+            if (!(code == 1 || (code == 2 && (pos & 63) < tv))) continue;
+            const float acc = G == 4 ? group_prob_sum4<DT>(dl[u], s_M, s_L)
+                                     : group_prob_sum<DT>(lg + (size_t)pos * G, G, s_M, s_L);
+            votes[pos] = dv[u] + rnd<DT>(acc / (float)G);
+        }
+    }
+    // ---- (E) Q windows: one warp per window, two tokens per lane
+    for (int blk = q_blk; blk < blk1; blk += nthr >> 5) {
+        const int slot = blk - n_mblk;
+        const T* wl = lg + ((size_t)g.S_cap + (size_t)slot * 64) * G;
+        if (blk != q_blk && G == 4) {
+            el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
+            el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
+        }
+        if (!s_live[blk - blk0]) continue;
+        const float a0 = G == 4 ? group_prob_sum4<DT>(el2[0], s_M, s_L)
+                                : group_prob_sum<DT>(wl + (size_t)lane * G, G, s_M, s_L);
+        const float a1 = G == 4 ? group_prob_sum4<DT>(el2[1], s_M, s_L)
+                                : group_prob_sum<DT>(wl + (size_t)(lane + 32) * G, G, s_M, s_L);
+        float a = rnd<DT>(a0 / (float)G) + rnd<DT>(a1 / (float)G);
+        a = warp_sum(a);
+        if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
+    }
+    sync();
+    // ---- output slice
     {
         const bool has_q = L.seq[b * 4 + 1] > 0;
         for (int el = e0 + tid; el < e1; el += nthr) {
@@ -267,45 +371,6 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
             const float om_ = s_acc[0][el], oq = s_acc[1][el];
             const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
             st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
-        }
-    }
-    // (D) main-zone tokens of this unit, four per thread per round with all
-    //     loads issued before any ledger store
-    const T* lg = reinterpret_cast<const T*>(logits) + (size_t)bh * S_tot * G;
-    float* votes = L.votes + bh * g.S_cap;
-    const int p_beg = blk0 * 64, p_end = min(blk1, n_mblk) * 64;
-    for (int base = p_beg + tid; base < p_end; base += 4 * nthr) {
-        bool lv[4];
-        float vo[4], acc[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int pos = base + u * nthr;
-            lv[u] = false;
-            if (pos < p_end) {
-                const int code = s_live[(pos >> 6) - blk0];
-                lv[u] = code == 1 || (code == 2 && (pos & 63) < tv);
-            }
-            if (lv[u]) {
-                acc[u] = group_prob_sum<DT>(lg + (size_t)pos * G, G, s_M, s_L);
-                vo[u] = votes[pos];
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-            if (lv[u]) votes[base + u * nthr] = vo[u] + rnd<DT>(acc[u] / (float)G);
-    }
-    // (E) Q windows of this unit: one warp per window, two tokens per lane
-    {
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int blk = max(blk0, n_mblk) + warp; blk < blk1; blk += nthr >> 5) {
-            if (!s_live[blk - blk0]) continue;
-            const int slot = blk - n_mblk;
-            const T* wl = lg + ((size_t)g.S_cap + (size_t)slot * 64) * G;
-            const float a0 = group_prob_sum<DT>(wl + (size_t)lane * G, G, s_M, s_L);
-            const float a1 = group_prob_sum<DT>(wl + (size_t)(lane + 32) * G, G, s_M, s_L);
-            float a = rnd<DT>(a0 / (float)G) + rnd<DT>(a1 / (float)G);
-            a = warp_sum(a);
-            if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
         }
     }
     sync();   // the scratch is reused by the next unit
@@ -318,26 +383,37 @@ struct ConsumerSync {
     __device__ void operator()() const { consumer_sync(); }
 };
 
+__device__ __forceinline__ int atom_add_acqrel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_add_release_gpu(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Barrier across all CTAs of a grid whose CTAs are all resident (cooperative
-// launch).  Called by one thread per CTA; count must be zero before the first
-// arrival (the last arrival resets it), gen may hold any value.  Gives up after
-// about two seconds and returns false.
+// launch).  Called by one thread per CTA after the CTA's threads have made
+// their global writes visible and synchronised; count must be zero before the
+// first arrival (the last arrival resets it), gen may hold any value.  The
+// arrival is an acquire-release add, the release of the waiters a release
+// add, the wait an acquire load.  Gives up after about two seconds and
+// returns false.
 __device__ __forceinline__ bool grid_barrier(int* count, int* gen, int n) {
-    volatile int* vgen = gen;
-    const int g0 = *vgen;
-    __threadfence();
-    if (atomicAdd(count, 1) == n - 1) {
+    const int g0 = *reinterpret_cast<volatile int*>(gen);
+    if (atom_add_acqrel_gpu(count, 1) == n - 1) {
         *count = 0;
-        __threadfence();
-        atomicAdd(gen, 1);
+        red_add_release_gpu(gen, 1);
         return true;
     }
     const uint64_t t0 = global_ns();
-    while (*vgen == g0) {
+    while (ld_acquire_gpu(gen) == g0)
         if (global_ns() - t0 > 2000000000ull) return false;
-        __nanosleep(64);
-    }
-    __threadfence();
     return true;
 }
 
@@ -353,11 +429,12 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     const int NS = P.ns;
     const int G = g.G;
     unsigned char* stages = smem;
-    float* s_q = reinterpret_cast<float*>(smem + NS * MM_STAGE);        // [8][128]
-    float* s_o = s_q + MM_G * 128;                                      // [CW][G][128]
-    float* s_m = s_o + MM_CW * G * 128;                                 // [CW][8]
-    float* s_l = s_m + MM_CW * MM_G;                                    // [CW][8]
-    uint64_t* full = reinterpret_cast<uint64_t*>(s_l + MM_CW * MM_G);
+    // per-warp segment states, double-buffered by segment parity
+    float* s_wo = reinterpret_cast<float*>(smem + NS * MM_STAGE);       // [2][CW][G][128]
+    float* s_wm = s_wo + 2 * MM_CW * G * 128;                           // [2][CW][8]
+    float* s_wl = s_wm + 2 * MM_CW * MM_G;                              // [2][CW][8]
+    int* s_cnt = reinterpret_cast<int*>(s_wl + 2 * MM_CW * MM_G);       // [2] arrivals, [2] merges done
+    uint64_t* full = reinterpret_cast<uint64_t*>(s_cnt + 4);
     uint64_t* empty = full + MM_MAXNS;
     unsigned char* s_skip = reinterpret_cast<unsigned char*>(empty + MM_MAXNS);
 
@@ -373,6 +450,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             mbar_init(&empty[s], 1);
         }
         fence_barrier_init();
+        s_cnt[0] = s_cnt[1] = s_cnt[2] = s_cnt[3] = 0;
     }
     // Which of this CTA's items hold no live token (the slot tables are not
     // written by the kernel that precedes this one, so read them before the wait).
@@ -462,27 +540,43 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 
     // q is written by the preceding kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Q^T fragments straight from global memory, per warp (no CTA barrier):
+    // lane (gq, t4) holds q[gq][16kk + 2t4 + {0,1}] and q[gq][16kk + 2t4 + {8,9}]
     auto load_q = [&](long long bh) {
         const int b = (int)(bh / g.H), h = (int)(bh % g.H);
-        consumer_sync();
-        for (int idx = threadIdx.x; idx < MM_G * 128; idx += MM_CW * 32) {
-            const int gi = idx >> 7, d = idx & 127;
-            s_q[idx] = gi < G ? ld<DT>(q, ((size_t)b * g.H * G + (size_t)h * G + gi) * 128 + d) : 0.f;
-        }
-        consumer_sync();
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(
+            reinterpret_cast<const T*>(q) + ((size_t)b * g.H * G + (size_t)h * G + (gq < G ? gq : 0)) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-            const float* qr = s_q + gq * 128 + 16 * kk + 2 * t4;
-            bq[kk][0] = pack2<DT>(qr[0], qr[1]);
-            bq[kk][1] = pack2<DT>(qr[8], qr[9]);
+            bq[kk][0] = gq < G ? __ldcg(qr + 8 * kk + t4) : 0u;
+            bq[kk][1] = gq < G ? __ldcg(qr + 8 * kk + t4 + 4) : 0u;
         }
     };
 
-    // Merge the warps' partials of one segment (the items of one (b, h, zone) in
-    // this CTA's range) and write it.
-    auto flush = [&](int key) {
+    // End of a segment (the items of one (b, h, zone) in this CTA's range) for
+    // this warp: its softmax state goes to a shared slot, and the last of the
+    // CTA's warps to arrive merges the slots and writes the CTA's partial.
+    // No CTA-wide barrier: warps move on to the next segment at once.  Slots
+    // are double-buffered by segment parity; a warp two segments ahead waits
+    // (bounded) until the older segment has been merged.
+    int seg = 0;
+    auto flush = [&](int key, bool final_seg) {
         const long long bh = key >> 1;
         const int zone = key & 1;
+        const int p = seg & 1;
+        if (lane == 0) {
+            volatile int* done = s_cnt + 2 + p;
+            if (*done < (seg >> 1)) {
+                const uint64_t t0 = global_ns();
+                while (*done < (seg >> 1)) {
+                    if (global_ns() - t0 > 2000000000ull) {
+                        set_err(L.err, QV_DERR_LAYOUT);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncwarp();
 #pragma unroll
         for (int col = 0; col < 2; ++col) {
 #pragma unroll
@@ -492,11 +586,15 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 svz[col] += __shfl_xor_sync(0xffffffffu, svz[col], off);
             }
         }
+        float* wo = s_wo + ((size_t)p * MM_CW + warp) * G * 128;
 #pragma unroll
         for (int col = 0; col < 2; ++col) {
             const int hh = 2 * t4 + col;
             if (hh < G) {
-                if (gq == 0) { s_m[warp * MM_G + hh] = m[col]; s_l[warp * MM_G + hh] = ls[col]; }
+                if (gq == 0) {
+                    s_wm[(p * MM_CW + warp) * MM_G + hh] = m[col];
+                    s_wl[(p * MM_CW + warp) * MM_G + hh] = ls[col];
+                }
 #pragma unroll
                 for (int dt = 0; dt < 8; ++dt) {
                     float va = o[dt][col], vb = o[dt][2 + col];
@@ -507,32 +605,83 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                         va = (va - 1024.f * spp[col]) * (1.f / 1024.f) + svz[col];
                         vb = (vb - 1024.f * spp[col]) * (1.f / 1024.f) + svz[col];
                     }
-                    s_o[(warp * G + hh) * 128 + da] = va;
-                    s_o[(warp * G + hh) * 128 + db] = vb;
+                    wo[hh * 128 + da] = va;
+                    wo[hh * 128 + db] = vb;
                 }
             }
         }
-        consumer_sync();
-        int first, cnt;
-        mm_zone_ctas(P, bh, zone, &first, &cnt);
-        float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
-        for (int idx = threadIdx.x; idx < G * 128; idx += MM_CW * 32) {
-            const int hh = idx >> 7, d = idx & 127;
-            float M = -INFINITY;
-            for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, s_m[w * MM_G + hh]);
-            float acc = 0.f, lsum = 0.f;
-            if (M > -INFINITY)
+        if (final_seg) {
+            // the CTA's last segment: every warp is here, so merge with all threads
+            consumer_sync();
+            int first, cnt;
+            mm_zone_ctas(P, bh, zone, &first, &cnt);
+            float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
+            const float* wm = s_wm + p * MM_CW * MM_G;
+            const float* wl = s_wl + p * MM_CW * MM_G;
+            const float* wo0 = s_wo + (size_t)p * MM_CW * G * 128;
+            for (int idx = threadIdx.x; idx < G * 128; idx += MM_CW * 32) {
+                const int hh = idx >> 7, d = idx & 127;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
+                float acc = 0.f, lsum = 0.f;
+#pragma unroll
                 for (int w = 0; w < MM_CW; ++w) {
-                    const float mw = s_m[w * MM_G + hh];
+                    const float mw = wm[w * MM_G + hh];
                     if (mw == -INFINITY) continue;
                     const float ew = __expf(mw - M);
-                    acc += s_o[(w * G + hh) * 128 + d] * ew;
-                    lsum += s_l[w * MM_G + hh] * ew;
+                    acc += wo0[((size_t)w * G + hh) * 128 + d] * ew;
+                    lsum += wl[w * MM_G + hh] * ew;
                 }
-            part[hh * 130 + 2 + d] = acc;
-            if (d == 0) { part[hh * 130] = M; part[hh * 130 + 1] = lsum; }
+                part[hh * 130 + 2 + d] = acc;
+                if (d == 0) { part[hh * 130] = M; part[hh * 130 + 1] = lsum; }
+            }
+            ++seg;
+            return;
         }
-        consumer_sync();
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(s_cnt + p, 1) == MM_CW - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            int first, cnt;
+            mm_zone_ctas(P, bh, zone, &first, &cnt);
+            float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
+            const float* wm = s_wm + p * MM_CW * MM_G;
+            const float* wl = s_wl + p * MM_CW * MM_G;
+            const float* wo0 = s_wo + (size_t)p * MM_CW * G * 128;
+            for (int hh = 0; hh < G; ++hh) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
+                float ew[MM_CW];
+                float lsum = 0.f;
+#pragma unroll
+                for (int w = 0; w < MM_CW; ++w) {
+                    const float mw = wm[w * MM_G + hh];
+                    ew[w] = mw == -INFINITY ? 0.f : __expf(mw - M);
+                    lsum += wl[w * MM_G + hh] * ew[w];
+                }
+#pragma unroll
+                for (int d = lane; d < 128; d += 32) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int w = 0; w < MM_CW; ++w)
+                        if (ew[w] != 0.f) acc += wo0[((size_t)w * G + hh) * 128 + d] * ew[w];
+                    part[hh * 130 + 2 + d] = acc;
+                }
+                if (lane == 0) { part[hh * 130] = M; part[hh * 130 + 1] = lsum; }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                s_cnt[p] = 0;
+                __threadfence_block();
+                atomicAdd(s_cnt + 2 + p, 1);
+            }
+        }
+        ++seg;
     };
 
     // online-softmax update for one column from this lane's NV logits
@@ -578,7 +727,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const int zone = j >= P.n_main ? 1 : 0;
         const int key = end ? -2 : (int)(bh * 2 + zone);
         if (key != cur_key) {
-            if (cur_key >= 0) flush(cur_key);
+            if (cur_key >= 0) flush(cur_key, end);
             if (end) break;
             if (bh != cur_bh) { load_q(bh); cur_bh = bh; }
             reset_acc();
@@ -690,14 +839,24 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const T* vz = reinterpret_cast<const T*>(stp + 16384 + 640);
             uint32_t bk[8][2];
             float zsum = 0.f, ssum = 0.f;
-            const float* qr = s_q + gq * 128;
+            // this lane needs q[gq][16kk + 4t4 + 0..3]: pairs held by quad lanes
+            // (2t4) & 3 and its neighbour, in register t4 >> 1
+            const int srcA = (lane & ~3) | ((2 * t4) & 3);
+            const bool hi_reg = (t4 >> 1) != 0;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 const int d0 = 16 * kk + 4 * t4;
+                const uint32_t r0 = __shfl_sync(0xffffffffu, bq[kk][0], srcA);
+                const uint32_t r1 = __shfl_sync(0xffffffffu, bq[kk][1], srcA);
+                const uint32_t r2 = __shfl_sync(0xffffffffu, bq[kk][0], srcA + 1);
+                const uint32_t r3 = __shfl_sync(0xffffffffu, bq[kk][1], srcA + 1);
+                const uint32_t qlo = hi_reg ? r1 : r0, qhi = hi_reg ? r3 : r2;
+                const float qvals[4] = {bits_to_f<DT>(qlo & 0xffffu), bits_to_f<DT>(qlo >> 16),
+                                        bits_to_f<DT>(qhi & 0xffffu), bits_to_f<DT>(qhi >> 16)};
                 float qs[4];
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
-                    const float qv = qr[d0 + jj];
+                    const float qv = qvals[jj];
                     qs[jj] = f16r(qv * Elt<DT>::f(ks[d0 + jj]));
                     zsum = fmaf(qv, Elt<DT>::f(kz[d0 + jj]), zsum);
                     ssum += qs[jj];
@@ -888,7 +1047,7 @@ bool mm_supported(const Geo& g) {
 }
 
 static size_t mm_fixed_smem(const Geo& g) {
-    return 1024 + (size_t)(MM_G * 128 + MM_CW * g.G * 128 + 2 * MM_CW * MM_G) * 4 + 2 * MM_MAXNS * 8 + MM_SKIPMAP;
+    return 1024 + (size_t)(2 * MM_CW * g.G * 128 + 4 * MM_CW * MM_G) * 4 + 16 + 2 * MM_MAXNS * 8 + MM_SKIPMAP;
 }
 
 MmPlan mm_plan(const Geo& g) {
