@@ -425,7 +425,10 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                   void* logits, MmPlan P, void* __restrict__ out, int fuse_chunks, int blocks_per_chunk) {
     using T = typename Elt<DT>::T;
     extern __shared__ unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned base (128-byte-swizzled TMA boxes); offsetting the
+    // shared array itself keeps every derived pointer a shared-memory pointer,
+    // so the compiler emits shared (not generic) loads, stores and atomics
+    unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int NS = P.ns;
     const int G = g.G;
     unsigned char* stages = smem;
@@ -521,6 +524,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     // --------------------------------------------------------------- consumers
     const int gq = lane >> 2, t4 = lane & 3, mi = lane >> 3;
     uint32_t bq[8][2];            // Q^T fragments (main zone)
+    uint32_t qq[8][2];            // the same q values in the Q-cache layout (see load_q)
     float o[8][4];                // O^T accumulators: 8 d-tiles x (2 rows x 2 heads)
     float m[2], ls[2], spp[2], svz[2];
     int cur_key = -1;
@@ -550,6 +554,19 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         for (int kk = 0; kk < 8; ++kk) {
             bq[kk][0] = gq < G ? __ldcg(qr + 8 * kk + t4) : 0u;
             bq[kk][1] = gq < G ? __ldcg(qr + 8 * kk + t4 + 4) : 0u;
+        }
+        // Q-cache windows need q[gq][16kk + 4t4 + 0..3] per lane: pairs held by
+        // quad lanes (2t4) & 3 and its neighbour, in register t4 >> 1
+        const int srcA = (lane & ~3) | ((2 * t4) & 3);
+        const bool hi_reg = (t4 >> 1) != 0;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t r0 = __shfl_sync(0xffffffffu, bq[kk][0], srcA);
+            const uint32_t r1 = __shfl_sync(0xffffffffu, bq[kk][1], srcA);
+            const uint32_t r2 = __shfl_sync(0xffffffffu, bq[kk][0], srcA + 1);
+            const uint32_t r3 = __shfl_sync(0xffffffffu, bq[kk][1], srcA + 1);
+            qq[kk][0] = hi_reg ? r1 : r0;
+            qq[kk][1] = hi_reg ? r3 : r2;
         }
     };
 
@@ -839,30 +856,29 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const T* vz = reinterpret_cast<const T*>(stp + 16384 + 640);
             uint32_t bk[8][2];
             float zsum = 0.f, ssum = 0.f;
-            // this lane needs q[gq][16kk + 4t4 + 0..3]: pairs held by quad lanes
-            // (2t4) & 3 and its neighbour, in register t4 >> 1
-            const int srcA = (lane & ~3) | ((2 * t4) & 3);
-            const bool hi_reg = (t4 >> 1) != 0;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
+                // lane (gq, t4): d = 16kk + 4t4 + 0..3; scales and zero points in
+                // one 8-byte load each
                 const int d0 = 16 * kk + 4 * t4;
-                const uint32_t r0 = __shfl_sync(0xffffffffu, bq[kk][0], srcA);
-                const uint32_t r1 = __shfl_sync(0xffffffffu, bq[kk][1], srcA);
-                const uint32_t r2 = __shfl_sync(0xffffffffu, bq[kk][0], srcA + 1);
-                const uint32_t r3 = __shfl_sync(0xffffffffu, bq[kk][1], srcA + 1);
-                const uint32_t qlo = hi_reg ? r1 : r0, qhi = hi_reg ? r3 : r2;
-                const float qvals[4] = {bits_to_f<DT>(qlo & 0xffffu), bits_to_f<DT>(qlo >> 16),
-                                        bits_to_f<DT>(qhi & 0xffffu), bits_to_f<DT>(qhi >> 16)};
-                float qs[4];
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    const float qv = qvals[jj];
-                    qs[jj] = f16r(qv * Elt<DT>::f(ks[d0 + jj]));
-                    zsum = fmaf(qv, Elt<DT>::f(kz[d0 + jj]), zsum);
-                    ssum += qs[jj];
-                }
-                bk[kk][0] = pack2<QV_F16>(qs[0], qs[1]);
-                bk[kk][1] = pack2<QV_F16>(qs[2], qs[3]);
+                const uint2 ksv = *reinterpret_cast<const uint2*>(ks + d0);
+                const uint2 kzv = *reinterpret_cast<const uint2*>(kz + d0);
+                const float q0 = bits_to_f<DT>(qq[kk][0] & 0xffffu), q1 = bits_to_f<DT>(qq[kk][0] >> 16);
+                const float q2 = bits_to_f<DT>(qq[kk][1] & 0xffffu), q3 = bits_to_f<DT>(qq[kk][1] >> 16);
+                // q * K scale rounded once to f16 (two values per conversion)
+                const __half2 h01 = __floats2half2_rn(q0 * bits_to_f<DT>(ksv.x & 0xffffu), q1 * bits_to_f<DT>(ksv.x >> 16));
+                const __half2 h23 = __floats2half2_rn(q2 * bits_to_f<DT>(ksv.y & 0xffffu), q3 * bits_to_f<DT>(ksv.y >> 16));
+                bk[kk][0] = *reinterpret_cast<const uint32_t*>(&h01);
+                bk[kk][1] = *reinterpret_cast<const uint32_t*>(&h23);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                zsum = fmaf(q0, bits_to_f<DT>(kzv.x & 0xffffu), zsum);
+                zsum = fmaf(q1, bits_to_f<DT>(kzv.x >> 16), zsum);
+                zsum = fmaf(q2, bits_to_f<DT>(kzv.y & 0xffffu), zsum);
+                zsum = fmaf(q3, bits_to_f<DT>(kzv.y >> 16), zsum);
+                ssum += f01.x;
+                ssum += f01.y;
+                ssum += f23.x;
+                ssum += f23.y;
             }
             zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
             zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
@@ -956,8 +972,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         // Combine in this grid (small batches): every CTA is resident, so after
         // a grid-wide barrier all partials and logits are visible and the
         // (b, h, chunk) units are spread over the CTAs.
+        // (the CTA barrier orders every consumer thread's partial and logit
+        // writes before thread 0's release arrival)
         __shared__ int s_pass;
-        __threadfence();
         consumer_sync();
         if (threadIdx.x == 0) {
             s_pass = grid_barrier(tickets + 1, tickets + 2, (int)gridDim.x) ? 1 : 0;
