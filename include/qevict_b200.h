@@ -178,6 +178,21 @@ int qv_decode_attention_noalloc(const qv_dims* d, const qv_layer* L, const void*
 int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
                    qv_stream_t stream);
 
+/* The eviction cycle of a layer whose KV heads are split over several devices
+ * (one qv_layer per device, dims.kv_heads = the local heads).  The cycle's one
+ * coupling between heads -- the number of Q-cache losers is the minimum over
+ * all heads of the candidates left after the top-k (eviction_manager.py:335-345)
+ * -- needs the heads of every device: qv_evict_cycle_count writes the local
+ * minimum per sequence (int32 [batch]) and changes nothing else; after a MIN
+ * reduction of those counts over the devices, qv_evict_cycle_ext runs the cycle
+ * with the global minimum.  On one device qv_evict_cycle is the same as
+ * count + ext with the local counts.  No counterpart in the reference, which
+ * keeps all heads of a layer on one device. */
+int qv_evict_cycle_count(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                         int32_t* loser_count, qv_stream_t stream);
+int qv_evict_cycle_ext(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                       const int32_t* loser_count, qv_stream_t stream);
+
 /* ---- prefill ----------------------------------------------------------- */
 
 /* Build the layer state from a prompt: window tally, top-k/top-q selection,

@@ -65,6 +65,8 @@ def lib():
         "qv_decode_attention_noalloc": (ctypes.c_int, [D, Lp, vp, vp, vp]),
         "qv_rope": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, i32, vp]),
         "qv_evict_cycle": (ctypes.c_int, [D, Lp, vp, sz, vp]),
+        "qv_evict_cycle_count": (ctypes.c_int, [D, Lp, vp, sz, vp, vp]),
+        "qv_evict_cycle_ext": (ctypes.c_int, [D, Lp, vp, sz, vp, vp]),
         "qv_prefill_build": (ctypes.c_int, [D, Lp, vp, vp, i32, vp, i32, vp]),
         "qv_prefill_attention": (ctypes.c_int, [D, vp, vp, vp, i32, vp, vp, vp, sz, vp]),
         "qv_prefill_workspace_bytes": (sz, [D, i32]),
@@ -89,6 +91,7 @@ def exported_symbols():
             "qv_decode_logits_offset",
             "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention",
             "qv_decode_attention_noalloc", "qv_evict_cycle",
+            "qv_evict_cycle_count", "qv_evict_cycle_ext",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_read_error",
             "qv_last_cuda_error", "qv_version"]

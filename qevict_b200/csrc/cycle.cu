@@ -54,7 +54,12 @@ static size_t select_smem_per_warp(const Geo& g) {
     return (size_t)NC * 14 * 4 + (size_t)(g.kw + g.R) * 4 + 64;
 }
 
-__global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, CycleWs ws, int per_warp_bytes) {
+// nrem_out != nullptr: counting pass only -- write, per sequence, the minimum
+// over this launch's KV heads of the loser count and change nothing else.
+// nrem_in != nullptr: the minimum over KV heads held elsewhere (other ranks of
+// a head-sharded layer), folded into this launch's own minimum.
+__global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, CycleWs ws, int per_warp_bytes,
+                                                            int32_t* nrem_out, const int32_t* nrem_in) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_nrem;
     const int b = blockIdx.x;
@@ -154,7 +159,7 @@ __global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, C
         for (int i = 0; i < vo; ++i) already |= (c_id[i] == last);
         const float gen = sbv(last);
         const float hist = lhist[last];
-        if (!already) lhist[last] = 0.f;
+        if (!already && !nrem_out) lhist[last] = 0.f;
         c_id[vo] = last;
         c_sc[vo] = already ? -INFINITY : gen + hist;
         c_src[vo] = (last >= L0 && last <= cw) ? last % g.R : -1;
@@ -199,6 +204,12 @@ __global__ void __launch_bounds__(1024) cycle_select_kernel(Geo g, qv_layer L, C
     for (int o = 16; o > 0; o >>= 1) nrem += __shfl_xor_sync(0xffffffffu, nrem, o);
     __syncthreads();
     if (lane == 0) atomicMin(&s_nrem, nrem);
+    __syncthreads();
+    if (nrem_out) {
+        if (threadIdx.x == 0) nrem_out[b] = s_nrem;
+        return;
+    }
+    if (nrem_in && threadIdx.x == 0) s_nrem = min(s_nrem, nrem_in[b]);
     __syncthreads();
     const int q_new = (g.qw > 0 && s_nrem > 0) ? min(g.qw, s_nrem) : 0;
 
@@ -457,8 +468,8 @@ static void launch_cycle_moves(const Geo& g, const qv_layer& L, const CycleWs& w
     cycle_up_scatter_kernel<DT><<<gu, 128, 0, s>>>(g, L, w);
 }
 
-extern "C" int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
-                              qv_stream_t stream) {
+static int cycle_launch(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                        int32_t* nrem_out, const int32_t* nrem_in, qv_stream_t stream) {
     int rc = validate_dims(d);
     if (rc) return rc;
     if (!L || !workspace || !L->step || !L->seq || !L->err) return QV_EINVAL;
@@ -476,11 +487,30 @@ extern "C" int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspa
     cudaError_t e = ensure_smem(cycle_select_kernel, smem, &cached);
     if (e != cudaSuccess) return set_cuda_error(e);
     cudaStream_t s = (cudaStream_t)stream;
-    cycle_select_kernel<<<g.B, 32 * g.H, smem, s>>>(g, *L, w, (int)per_warp);
-    switch (g.dt) {
-        case QV_F32: launch_cycle_moves<QV_F32>(g, *L, w, s); break;
-        case QV_BF16: launch_cycle_moves<QV_BF16>(g, *L, w, s); break;
-        default: launch_cycle_moves<QV_F16>(g, *L, w, s); break;
+    cycle_select_kernel<<<g.B, 32 * g.H, smem, s>>>(g, *L, w, (int)per_warp, nrem_out, nrem_in);
+    if (!nrem_out) {
+        switch (g.dt) {
+            case QV_F32: launch_cycle_moves<QV_F32>(g, *L, w, s); break;
+            case QV_BF16: launch_cycle_moves<QV_BF16>(g, *L, w, s); break;
+            default: launch_cycle_moves<QV_F16>(g, *L, w, s); break;
+        }
     }
     return check_launch();
+}
+
+extern "C" int qv_evict_cycle(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                              qv_stream_t stream) {
+    return cycle_launch(d, L, workspace, workspace_bytes, nullptr, nullptr, stream);
+}
+
+extern "C" int qv_evict_cycle_count(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                                    int32_t* loser_count, qv_stream_t stream) {
+    if (!loser_count) return QV_EINVAL;
+    return cycle_launch(d, L, workspace, workspace_bytes, loser_count, nullptr, stream);
+}
+
+extern "C" int qv_evict_cycle_ext(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                                  const int32_t* loser_count, qv_stream_t stream) {
+    if (!loser_count) return QV_EINVAL;
+    return cycle_launch(d, L, workspace, workspace_bytes, nullptr, loser_count, stream);
 }
