@@ -1,4 +1,6 @@
 // Prefill lane: causal attention + per-key column sums that seed the ledger.
+// This file holds the CUDA-core kernels, used for fp32; bf16/fp16 run the
+// tensor-core kernels of prefill_tc.cu (same results, within rounding).
 //
 // Replaces flash_attn_func + compute_chunked_prefill_scores
 // (src/models/attention/ops_flash.py:22-141).  Logits are rounded the way the
@@ -238,6 +240,11 @@ prefill_colsum_kernel(Geo g, const void* __restrict__ q, const void* __restrict_
     if (tid < PT && k0 + tid < S) colsum[((size_t)b * g.H + h) * S + k0 + tid] = sAcc[tid];
 }
 
+// tensor-core prefill lane (prefill_tc.cu) for bf16/fp16
+bool pft_supported(const Geo& g);
+int pft_launch(const Geo& g, const void* q, const void* k, const void* v, int S, void* out, float* colsum,
+               float* stats, int* err, cudaStream_t s);
+
 static size_t fwd_smem(int D) { return (size_t)(2 * PT * (D + 1) + PT * D + PT * (PT + 1) + PT) * 4; }
 static size_t col_smem(int D) { return (size_t)(2 * PT * (D + 1) + 2 * PT + 16 * PT + 2 * PT) * 4; }
 
@@ -278,6 +285,7 @@ extern "C" int qv_prefill_attention(const qv_dims* d, const void* q, const void*
     Geo g = make_geo(d);
     float* stats = reinterpret_cast<float*>(workspace);
     cudaStream_t s = (cudaStream_t)stream;
+    if (pft_supported(g)) return pft_launch(g, q, k, v, S, out, colsum, stats, nullptr, s);
 #define QV_PA(DT)                                                                   \
     return g.D == 128 ? launch_prefill<DT, 128>(g, q, k, v, S, out, colsum, stats, s) \
                       : launch_prefill<DT, 64>(g, q, k, v, S, out, colsum, stats, s)
