@@ -379,50 +379,12 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
 struct BlockSync {
     __device__ void operator()() const { __syncthreads(); }
 };
-struct ConsumerSync {
-    __device__ void operator()() const { consumer_sync(); }
-};
-
-__device__ __forceinline__ int atom_add_acqrel_gpu(int* p, int v) {
-    int old;
-    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-__device__ __forceinline__ void red_add_release_gpu(int* p, int v) {
-    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Barrier across all CTAs of a grid whose CTAs are all resident (cooperative
-// launch).  Called by one thread per CTA after the CTA's threads have made
-// their global writes visible and synchronised; count must be zero before the
-// first arrival (the last arrival resets it), gen may hold any value.  The
-// arrival is an acquire-release add, the release of the waiters a release
-// add, the wait an acquire load.  Gives up after about two seconds and
-// returns false.
-__device__ __forceinline__ bool grid_barrier(int* count, int* gen, int n) {
-    const int g0 = *reinterpret_cast<volatile int*>(gen);
-    if (atom_add_acqrel_gpu(count, 1) == n - 1) {
-        *count = 0;
-        red_add_release_gpu(gen, 1);
-        return true;
-    }
-    const uint64_t t0 = global_ns();
-    while (ld_acquire_gpu(gen) == g0)
-        if (global_ns() - t0 > 2000000000ull) return false;
-    return true;
-}
-
 template <int DT>
 __global__ void __launch_bounds__(MM_THREADS, 1)
 decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ CUtensorMap tmKQ, const __grid_constant__ CUtensorMap tmVQ,
                   Geo g, qv_layer L, const void* __restrict__ q, int* tickets, float* partial,
-                  void* logits, MmPlan P, void* __restrict__ out, int fuse_chunks, int blocks_per_chunk) {
+                  void* logits, MmPlan P) {
     using T = typename Elt<DT>::T;
     extern __shared__ unsigned char smem_raw[];
     // 1024-byte aligned base (128-byte-swizzled TMA boxes); offsetting the
@@ -968,29 +930,6 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (fuse_chunks > 0) {
-        // Combine in this grid (small batches): every CTA is resident, so after
-        // a grid-wide barrier all partials and logits are visible and the
-        // (b, h, chunk) units are spread over the CTAs.
-        // (the CTA barrier orders every consumer thread's partial and logit
-        // writes before thread 0's release arrival)
-        __shared__ int s_pass;
-        consumer_sync();
-        if (threadIdx.x == 0) {
-            s_pass = grid_barrier(tickets + 1, tickets + 2, (int)gridDim.x) ? 1 : 0;
-            if (!s_pass) set_err(L.err, QV_DERR_LAYOUT);
-            // every CTA read the token counter before arriving
-            else if (c == 0) L.step[0] = N0 + 1;
-        }
-        consumer_sync();
-        if (!s_pass) return;
-        float* sm = reinterpret_cast<float*>(stages);
-        const int units = fuse_chunks * g.B * g.H;
-        for (int u = c; u < units; u += (int)gridDim.x)
-            combine_unit<DT>(g, L, out, partial, logits, P, N0, u / fuse_chunks, u % fuse_chunks, fuse_chunks,
-                             blocks_per_chunk, sm, (int)threadIdx.x, MM_CW * 32, ConsumerSync{});
-        return;
-    }
     // let the combine grid get scheduled while this grid drains (it waits for
     // this grid's completion before reading anything)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1006,9 +945,8 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     }
 }
 
-// Separate combine kernel (used when the batch is large enough that a
-// dedicated grid of many small blocks beats the attention kernel's own CTAs).
-// grid = (chunks, B*H); chunk 0..chunks-1 of each (b, h).
+// Combine kernel: a grid of many small blocks, chained to the attention
+// kernel with programmatic dependent launch.  grid = (chunks, B*H).
 template <int DT>
 __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, void* __restrict__ out,
                                                              const float* __restrict__ partial,
@@ -1119,41 +1057,33 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     void* lgt = base + ol;
     const int BH = g.B * g.H;
     const int n_blk = g.S_cap / 64 + g.qw;
-    // Small batches combine inside the attention grid after a grid-wide barrier
-    // (one launch, no second-kernel tail); large ones use a separate grid of
-    // many small blocks, chained with programmatic dependent launch.
-    const bool fuse = BH <= P.nC;
-    int chunks = fuse ? P.nC / BH : (2 * sm_count() + BH - 1) / BH;
+    int chunks = (2 * sm_count() + BH - 1) / BH;
     if (chunks > n_blk) chunks = n_blk;
     if (chunks < (n_blk + MM_CMB_MAXBLK - 1) / MM_CMB_MAXBLK) chunks = (n_blk + MM_CMB_MAXBLK - 1) / MM_CMB_MAXBLK;
     if (chunks < 1) chunks = 1;
     const int bpc = (n_blk + chunks - 1) / chunks;
     chunks = (n_blk + bpc - 1) / bpc;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeCooperative;
-    attr[1].val.cooperative = 1;
     cudaLaunchConfig_t cfg1 = {};
     cfg1.gridDim = dim3(P.nC);
     cfg1.blockDim = dim3(MM_THREADS);
     cfg1.dynamicSmemBytes = smem;
     cfg1.stream = s;
     cfg1.attrs = attr;
-    cfg1.numAttrs = fuse ? 2 : 1;
+    cfg1.numAttrs = 1;
     cudaLaunchConfig_t cfg2 = cfg1;
     cfg2.gridDim = dim3(chunks, BH);
     cfg2.blockDim = dim3(256);
     cfg2.dynamicSmemBytes = 0;
-    cfg2.numAttrs = 1;
-    const int fchunks = fuse ? chunks : 0;
     auto kern = g.dt == QV_BF16 ? decode_mma_kernel<QV_BF16> : decode_mma_kernel<QV_F16>;
     auto comb = g.dt == QV_BF16 ? decode_combine_kernel<QV_BF16> : decode_combine_kernel<QV_F16>;
     cudaError_t e = ensure_smem(kern, smem, &cached[g.dt == QV_BF16 ? 1 : 2]);
     if (e != cudaSuccess) return set_cuda_error(e);
-    e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P, out, fchunks, bpc);
+    e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
     if (e != cudaSuccess) return set_cuda_error(e);
-    if (!fuse) e = cudaLaunchKernelEx(&cfg2, comb, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
+    e = cudaLaunchKernelEx(&cfg2, comb, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
     if (e != cudaSuccess) return set_cuda_error(e);
     return check_launch();
 }

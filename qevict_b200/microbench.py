@@ -57,8 +57,13 @@ def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=Fal
         st.step(q, kn, vn, out=out)
     torch.cuda.synchronize()
     attn_t, cyc_t, step_t, tvals = [], [], [], []
+    # a buffer larger than the 126 MB L2, rewritten before every step so that the
+    # cache arrives cold, as it does in a model where the weights stream between
+    # two launches of a layer
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     for _ in range(steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        flush.zero_()
         torch.cuda._sleep(2000000)
         ev[0].record()
         qr = st.append(q, kn, vn)
