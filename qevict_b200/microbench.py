@@ -13,6 +13,7 @@ per-sequence cache of 64 sink + 512 local + 2048 sticky BF16 tokens and 4096
 INT8 Q-cache tokens, 1000 steps.
 
     python -m qevict_b200.microbench [--batch 64] [--steps 1000] [--sticky 32] [--qwin 64]
+    python -m qevict_b200.microbench --prefill 8192 [--steps 5]   (one layer's prefill lane)
 """
 
 import argparse
@@ -97,6 +98,33 @@ def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=Fal
     return res
 
 
+def run_prefill(S=8192, batch=1, steps=5, quiet=False, dtype=torch.bfloat16):
+    """One layer's prefill lane (causal attention + column sums) at the Llama-3-8B
+    layer shape; reports ms per layer and TFLOP/s of the minimal causal
+    contraction count 2 * S^2 * D * Hq (Q.K^T and P.V over the lower triangle)."""
+    from .model import prefill_attention
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    Hq = H * G
+    q = torch.randn(batch, S, Hq, D, generator=g, device="cuda").to(dtype)
+    k = torch.randn(batch, S, H, D, generator=g, device="cuda").to(dtype)
+    v = torch.randn(batch, S, H, D, generator=g, device="cuda").to(dtype)
+    prefill_attention(q, k, v)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        prefill_attention(q, k, v)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    flops = 2.0 * S * S * D * Hq * batch
+    res = {"prefill_tokens": S, "batch": batch, "ms_per_layer": ms, "tflops_causal": flops / (ms * 1e-3) / 1e12}
+    if not quiet:
+        print(json.dumps(res))
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=64)
@@ -105,7 +133,11 @@ def main():
     ap.add_argument("--sticky", type=int, default=32)
     ap.add_argument("--qwin", type=int, default=64)
     ap.add_argument("--local", type=int, default=512)
+    ap.add_argument("--prefill", type=int, default=0, help="time one layer's prefill lane at this prompt length")
     a = ap.parse_args()
+    if a.prefill:
+        run_prefill(a.prefill, steps=max(1, min(a.steps, 20)))
+        return
     run(a.batch, a.steps, a.warmup, a.sticky, a.qwin, a.local)
 
 
