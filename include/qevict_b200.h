@@ -231,6 +231,18 @@ int qv_dequantize(int32_t n, int32_t omega, int32_t head_dim, int32_t bits, int3
                   int32_t per_token, const uint8_t* codes, const void* scale, const void* zp,
                   void* out, qv_stream_t stream);
 
+/* ---- elementwise steps of the full-model decode driver --------------------
+ * Not part of the reference's Sticky-KV path (its Llama layer uses HF
+ * modules); fused so that a decode step launches fewer small kernels.
+ * bf16, cols a multiple of 8, 16-byte aligned rows.
+ * qv_add_rmsnorm: x[r] = bf16(x[r] + delta[r]) (skipped when delta is NULL),
+ *                 h_out[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * weight); cols <= 16384.
+ * qv_silu_mul:    out[r] = bf16(bf16(SiLU(g)) * u) with g = gate_up[r][0:cols],
+ *                 u = gate_up[r][cols:2*cols]. */
+int qv_add_rmsnorm(int32_t rows, int32_t cols, void* x, const void* delta, const void* weight, float eps,
+                   void* h_out, qv_stream_t stream);
+int qv_silu_mul(int32_t rows, int32_t cols, const void* gate_up, void* out, qv_stream_t stream);
+
 /* ---- diagnostics ------------------------------------------------------- */
 int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* synchronises the stream */
 const char* qv_last_cuda_error(void);

@@ -1,11 +1,13 @@
 """A lean Llama-3-shaped decoder whose attention is the Sticky-KV hot path.
 
 Used for the full-model decode workload (Llama-3-8B shape: 32 layers, hidden
-4096, 32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256).  The
-projections, norms and MLP are plain cuBLAS/torch ops; attention runs the
-sm_100a kernels: RoPE + append, fused split-K decode attention with the ledger
-fold, the eviction cycle every omega tokens, and the prefill lane (causal
-attention + column sums -> state build).
+4096, 32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256).  A decode
+step per layer: cuBLAS projections into preallocated buffers, with the
+elementwise work between them fused (qv_add_rmsnorm: residual add + the next
+RMSNorm; qv_silu_mul: the MLP activation); attention runs the sm_100a
+kernels: RoPE + append, fused decode attention with the ledger fold, and the
+eviction cycle every omega tokens.  The prefill (prompt) path is torch/cuBLAS
+around the prefill lane (causal attention + column sums -> state build).
 
 Decode steps are captured in two CUDA graphs (a plain step and a step that
 ends an omega-window and runs the eviction cycle of every layer); all
@@ -124,6 +126,13 @@ class StickyLlamaDecoder:
         self.tok = torch.zeros(batch, dtype=torch.long, device=self.device)
         self.next_tok = torch.zeros(batch, dtype=torch.long, device=self.device)
         self.attn_out = torch.empty(batch, Hq, D, dtype=dtype, device=self.device)
+        # decode-step buffers (graph inputs/outputs)
+        self.x = torch.empty(batch, s.hidden, dtype=dtype, device=self.device)
+        self.h = torch.empty_like(self.x)
+        self.proj = torch.empty_like(self.x)
+        self.qkv = torch.empty(batch, (Hq + 2 * H) * D, dtype=dtype, device=self.device)
+        self.gu = torch.empty(batch, 2 * s.ffn, dtype=dtype, device=self.device)
+        self.act = torch.empty(batch, s.ffn, dtype=dtype, device=self.device)
         self.graphs = {}
 
     # ---------------------------------------------------------------- prefill
@@ -165,28 +174,42 @@ class StickyLlamaDecoder:
         return x + (F.silu(g) * u) @ L["wd"].t()
 
     # ----------------------------------------------------------------- decode
-    def _layer_step(self, li, x):
+    def _add_norm(self, delta, weight):
+        """x += delta (if given); h = RMSNorm(x) * weight (qv_add_rmsnorm)."""
+        rc = N.lib().qv_add_rmsnorm(self.B, self.s.hidden, N.ptr(self.x), N.ptr(delta), N.ptr(weight),
+                                    self.s.rms_eps, N.ptr(self.h), torch.cuda.current_stream(self.device).cuda_stream)
+        N.check(rc, "qv_add_rmsnorm")
+
+    def _layer_step(self, li):
+        """One decoder layer on self.x; expects self.h = RMSNorm(x) * ln1 and leaves
+        self.h = RMSNorm(x_out) * (the next layer's ln1, or the final norm)."""
         s, L, st = self.s, self.layers[li], self.states[li]
         B = self.B
         Hq, H, D = s.heads, s.kv_heads, s.head_dim
-        h = F.rms_norm(x, (s.hidden,), L["ln1"], s.rms_eps)
-        qkv = h @ L["wqkv"].t()
-        q = qkv[:, :Hq * D].reshape(B, Hq, D)
-        k = qkv[:, Hq * D:(Hq + H) * D].reshape(B, H, D)
-        v = qkv[:, (Hq + H) * D:].reshape(B, H, D)
+        torch.mm(self.h, L["wqkv"].t(), out=self.qkv)
+        q = self.qkv[:, :Hq * D].view(B, Hq, D)
+        k = self.qkv[:, Hq * D:(Hq + H) * D].view(B, H, D)
+        v = self.qkv[:, (Hq + H) * D:].view(B, H, D)
         qr = st.append(q, k, v, self.cos, self.sin)
         st.attend(qr, self.attn_out)
-        x = x + self.attn_out.reshape(B, Hq * D) @ L["wo"].t()
-        return self._mlp(x, L)
+        torch.mm(self.attn_out.view(B, Hq * D), L["wo"].t(), out=self.proj)
+        self._add_norm(self.proj, L["ln2"])
+        torch.mm(self.h, L["wgu"].t(), out=self.gu)
+        rc = N.lib().qv_silu_mul(B, s.ffn, N.ptr(self.gu), N.ptr(self.act),
+                                 torch.cuda.current_stream(self.device).cuda_stream)
+        N.check(rc, "qv_silu_mul")
+        torch.mm(self.act, L["wd"].t(), out=self.proj)
+        nxt = self.layers[li + 1]["ln1"] if li + 1 < s.layers else self.norm
+        self._add_norm(self.proj, nxt)
 
     def _step_body(self, cycle):
-        x = self.embed[self.tok]
+        torch.index_select(self.embed, 0, self.tok, out=self.x)
+        self._add_norm(None, self.layers[0]["ln1"])
         for li in range(self.s.layers):
-            x = self._layer_step(li, x)
+            self._layer_step(li)
             if cycle:
                 self.states[li].evict_cycle()
-        h = F.rms_norm(x, (self.s.hidden,), self.norm, self.s.rms_eps)
-        self.next_tok.copy_(torch.argmax(h @ self.lm_head.t(), dim=-1))
+        self.next_tok.copy_(torch.argmax(self.h @ self.lm_head.t(), dim=-1))
         self.tok.copy_(self.next_tok)
 
     def cycle_next(self):
