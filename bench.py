@@ -243,8 +243,10 @@ def run_ours(args):
     del ids
 
     W, K = args.warmup, args.steps
-    # per layer: rope_append_kernel, decode_mma_kernel, decode_combine_kernel
-    launches_per_step = 3 * model.s.layers
+    # per layer: rope_append_kernel, decode_mma_kernel, decode_combine_kernel,
+    # add_rmsnorm_kernel x2, silu_mul_kernel; per step: the first add_rmsnorm_kernel
+    # and argmax_kernel
+    launches_per_step = 6 * model.s.layers + 2
     # warm-up: eager first (allocator / cuBLAS), then graph capture, then graph replays
     n_eager = min(3, W)
     for _ in range(n_eager):

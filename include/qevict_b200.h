@@ -242,6 +242,13 @@ int qv_dequantize(int32_t n, int32_t omega, int32_t head_dim, int32_t bits, int3
 int qv_add_rmsnorm(int32_t rows, int32_t cols, void* x, const void* delta, const void* weight, float eps,
                    void* h_out, qv_stream_t stream);
 int qv_silu_mul(int32_t rows, int32_t cols, const void* gate_up, void* out, qv_stream_t stream);
+/* qv_argmax: out[r] = the index of the largest bf16 value of x[r] (smallest
+ * index among equal values), one launch.  The workspace
+ * (qv_argmax_workspace_bytes) must be zero before the first call; each call
+ * leaves it zero. */
+size_t qv_argmax_workspace_bytes(int32_t rows);
+int qv_argmax(int32_t rows, int32_t cols, const void* x, int64_t* out, void* workspace, size_t workspace_bytes,
+              qv_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------- */
 int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* synchronises the stream */

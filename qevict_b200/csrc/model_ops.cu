@@ -6,6 +6,7 @@
 //                    the next one, one kernel instead of two)
 //   qv_silu_mul      out = SiLU(g) * u of a [g | u] row (the MLP activation,
 //                    one kernel instead of two)
+//   qv_argmax        greedy token of each logit row in one launch
 //
 // bf16 in and out, fp32 arithmetic, rounded where the separate torch ops
 // round (the sum, SiLU(g), the product, the norm output).  One CTA per token
@@ -108,9 +109,72 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(int F, int rows, const __
     reinterpret_cast<uint4*>(out + (size_t)b * F)[c] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Greedy argmax of bf16 rows: blocks reduce slices of a row to (value, index),
+// then one 64-bit atomicMax per block on a key that orders by value and, among
+// equal values, by the smaller index; the last block of the row writes the
+// index and resets the row's key and ticket.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    const uint32_t b = v == 0.f ? 0u : __float_as_uint(v);   // -0 ties with +0
+    const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)o << 32) | (uint32_t)(0x7fffffff - i);
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(int cols, const __nv_bfloat16* __restrict__ x,
+                                                     unsigned long long* keys, int* tickets, int64_t* out) {
+    const int b = blockIdx.y;
+    const int per = (cols + gridDim.x - 1) / gridDim.x;
+    const int c0 = blockIdx.x * per, c1 = min(c0 + per, cols);
+    const __nv_bfloat16* row = x + (size_t)b * cols;
+    unsigned long long best = 0ull;
+    for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
+        const unsigned long long k = argmax_key(__bfloat162float(row[c]), c);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    __shared__ unsigned long long red[8];
+    __shared__ bool last;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        best = red[0] > best ? red[0] : best;
+        atomicMax(keys + b, best);
+        __threadfence();
+        last = atomicAdd(tickets + b, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        const unsigned long long k = atomicExch(keys + b, 0ull);
+        out[b] = (int64_t)(0x7fffffff - (int)(uint32_t)(k & 0xffffffffull));
+        tickets[b] = 0;
+    }
+}
+
 }  // namespace qv
 
 using namespace qv;
+
+extern "C" size_t qv_argmax_workspace_bytes(int32_t rows) {
+    return rows > 0 ? (size_t)rows * 16 : 0;
+}
+
+extern "C" int qv_argmax(int32_t rows, int32_t cols, const void* x, int64_t* out, void* workspace,
+                         size_t workspace_bytes, qv_stream_t stream) {
+    if (rows <= 0 || cols <= 0 || !x || !out || !workspace) return QV_EINVAL;
+    if (workspace_bytes < qv_argmax_workspace_bytes(rows)) return QV_ESPACE;
+    unsigned long long* keys = static_cast<unsigned long long*>(workspace);
+    int* tickets = reinterpret_cast<int*>(keys + rows);
+    int blocks = (cols + 2047) / 2048;
+    if (blocks > 148) blocks = 148;
+    argmax_kernel<<<dim3(blocks, rows), 256, 0, (cudaStream_t)stream>>>(cols, static_cast<const __nv_bfloat16*>(x),
+                                                                         keys, tickets, out);
+    return check_launch();
+}
 
 static bool mo_aligned(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 

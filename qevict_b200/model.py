@@ -6,7 +6,8 @@ step per layer: cuBLAS projections into preallocated buffers, with the
 elementwise work between them fused (qv_add_rmsnorm: residual add + the next
 RMSNorm; qv_silu_mul: the MLP activation); attention runs the sm_100a
 kernels: RoPE + append, fused decode attention with the ledger fold, and the
-eviction cycle every omega tokens.  The prefill (prompt) path is torch/cuBLAS
+eviction cycle every omega tokens; the LM head's greedy token comes from one
+argmax kernel (qv_argmax).  The prefill (prompt) path is torch/cuBLAS
 around the prefill lane (causal attention + column sums -> state build).
 
 Decode steps are captured in two CUDA graphs (a plain step and a step that
@@ -133,6 +134,9 @@ class StickyLlamaDecoder:
         self.qkv = torch.empty(batch, (Hq + 2 * H) * D, dtype=dtype, device=self.device)
         self.gu = torch.empty(batch, 2 * s.ffn, dtype=dtype, device=self.device)
         self.act = torch.empty(batch, s.ffn, dtype=dtype, device=self.device)
+        self.logits = torch.empty(batch, s.vocab, dtype=dtype, device=self.device)
+        self.argmax_ws = torch.zeros(int(N.lib().qv_argmax_workspace_bytes(batch)), dtype=torch.uint8,
+                                     device=self.device)
         self.graphs = {}
 
     # ---------------------------------------------------------------- prefill
@@ -209,7 +213,10 @@ class StickyLlamaDecoder:
             self._layer_step(li)
             if cycle:
                 self.states[li].evict_cycle()
-        self.next_tok.copy_(torch.argmax(self.h @ self.lm_head.t(), dim=-1))
+        torch.mm(self.h, self.lm_head.t(), out=self.logits)
+        rc = N.lib().qv_argmax(self.B, self.s.vocab, N.ptr(self.logits), N.ptr(self.next_tok), N.ptr(self.argmax_ws),
+                               self.argmax_ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
+        N.check(rc, "qv_argmax")
         self.tok.copy_(self.next_tok)
 
     def cycle_next(self):

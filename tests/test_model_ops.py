@@ -71,3 +71,20 @@ def test_small_decoder_graph_matches_eager():
         toks.append(torch.stack(out).cpu())
         assert all(st.read_error() == 0 for st in m.states)
     assert torch.equal(toks[0], toks[1])
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 128256), (3, 1000)])
+def test_argmax(rows, cols):
+    g = torch.Generator(device="cuda").manual_seed(cols)
+    x = torch.randn(rows, cols, generator=g, device="cuda").to(torch.bfloat16)
+    x[0, cols // 3] = 9.0          # a tie between two positions: the smaller index wins
+    x[0, cols // 2] = 9.0
+    ws = torch.zeros(int(N.lib().qv_argmax_workspace_bytes(rows)), dtype=torch.uint8, device="cuda")
+    out = torch.empty(rows, dtype=torch.int64, device="cuda")
+    for _ in range(2):             # the workspace is left reusable
+        rc = N.lib().qv_argmax(rows, cols, N.ptr(x), N.ptr(out), N.ptr(ws), ws.numel(),
+                               torch.cuda.current_stream().cuda_stream)
+        N.check(rc, "qv_argmax")
+        assert torch.equal(out, torch.argmax(x.float(), dim=1))
+        assert int(out[0]) == cols // 3
+
