@@ -250,6 +250,33 @@ size_t qv_argmax_workspace_bytes(int32_t rows);
 int qv_argmax(int32_t rows, int32_t cols, const void* x, int64_t* out, void* workspace, size_t workspace_bytes,
               qv_stream_t stream);
 
+/* ---- research token ledger (TrackingManager, kv_cache/tracking_manager.py:27-204)
+ * One sequence per call.  ledger [max_context][2 + 2*heads] float32 rows of
+ * (global id, layer id, physical position per head, cumulative importance per
+ * head), history [max_context][heads] float32 (the reference's
+ * _global_score_history), both -1 when fresh.  Positions index the
+ * reference's physical cache order.  Bit-identical to the reference's float32
+ * updates.
+ * qv_track_prefill replaces TrackingManager.record_prefill (tracking_manager.py:61-124):
+ *   importance [heads][kv_len] = attn_score_cache[0, :, :seq_len, :].sum(dim=1)
+ *   as float32; survivors [heads][n_surv] = the kept physical indices in
+ *   compressed order (eviction.py:225-229).
+ * qv_track_decode replaces TrackingManager.record_decode (tracking_manager.py:126-160):
+ *   scores [heads][kv_len] = attn_score_cache[0, :, 0, :] as float32; counter
+ *   is the global token counter after this token's increment.
+ * qv_track_positions replaces TrackingManager.update_physical_positions
+ *   (tracking_manager.py:162-191): mapping [heads][seq_len] old -> new
+ *   position (-1 = left the cache, cache.py:456-573), votes [heads][votes_stride]
+ *   the vote ledger the cycle consumed. */
+int qv_track_prefill(int32_t max_context, int32_t heads, int32_t seq_len, int32_t q_len, int32_t layer_idx,
+                     int64_t global_start, int32_t num_new, const float* importance, int32_t kv_len,
+                     const int64_t* survivors, int32_t n_surv, float* ledger, float* history, qv_stream_t stream);
+int qv_track_decode(int32_t max_context, int32_t heads, int64_t counter, int64_t global_start, int32_t seq_len,
+                    int32_t layer_idx, const float* scores, int32_t kv_len, float* ledger, float* history,
+                    qv_stream_t stream);
+int qv_track_positions(int32_t max_context, int32_t heads, int64_t counter, int32_t seq_len, const float* mapping,
+                       const float* votes, int32_t votes_stride, float* ledger, float* history, qv_stream_t stream);
+
 /* ---- diagnostics ------------------------------------------------------- */
 int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* synchronises the stream */
 const char* qv_last_cuda_error(void);

@@ -4,7 +4,8 @@ One sequence (the reference is batch-1), all KV heads of one layer, in the
 reference's own physical layout.  Mirrors, function by function:
 
   STICKYKVCache_LayerWise.__call__            src/models/kv_cache/cache.py:234-427
-  STICKYKVCache_LayerWise._build_physical_cache   cache.py:433-575
+  STICKYKVCache_LayerWise._build_physical_cache   cache.py:433-575 (with its
+                                              old -> new position mapping)
   EvictionManager.tally_prefill_scores        src/models/kv_cache/eviction_manager.py:115-173
   EvictionManager.commit_prefill_result       eviction_manager.py:184-192
   EvictionManager.tally_decode_scores         eviction_manager.py:198-203
@@ -123,6 +124,9 @@ class OracleStickyLayer:
         self.oob_qcache_b_drops = 0
         self.oob_qcache_c_drops = 0
         self.last_result = None
+        self.last_survivors = None    # prefill survivor positions [H, N] (eviction.py:225-229)
+        self.last_mapping = None      # last cycle's old -> new positions [H, S]
+        self.last_cycle_votes = None  # the vote ledger the last cycle consumed [H, S]
 
     def window_to_token(self, ids):
         return self.sink + np.asarray(ids, np.int64)[..., None] * self.omega + np.arange(self.omega)
@@ -228,6 +232,7 @@ class OracleStickyLayer:
             parts.append(np.broadcast_to(np.arange(score_end, S), (H, S - score_end)))
         allidx = np.clip(np.concatenate(parts, axis=1), 0, S - 1)
         surv = np.sort(allidx, axis=1)
+        self.last_survivors = surv
         hh = np.arange(H)[:, None]
         Kn, Vn = K[hh, surv], V[hh, surv]
         # commit_prefill_result (eviction_manager.py:184-192)
@@ -476,9 +481,14 @@ class OracleStickyLayer:
         else:
             found = np.zeros((H, ck), bool)
             first = np.zeros((H, ck), np.int64)
+        # mapping: old physical position -> new one, -1 when the token left the
+        # main zone (the token-ledger input, cache.py:456,509-510,527-528,542-557,570-573)
+        mp = np.full((H, S), -1.0, np.float32)
         nk[:, :sink] = K[:, :sink]
         nv[:, :sink] = V[:, :sink]
         nl[:, :sink] = self.lid[:, :sink]
+        mp[:, :sink] = np.arange(sink, dtype=np.float32)[None, :]
+        ar = np.arange(om, dtype=np.float32)
         for h in range(H):
             for i in range(ck):
                 npos = sink + i * om
@@ -488,18 +498,23 @@ class OracleStickyLayer:
                     nk[h, npos:npos + om] = K[h, fp:fp + om]
                     nv[h, npos:npos + om] = V[h, fp:fp + om]
                     nl[h, npos:npos + om] = wid
+                    mp[h, fp:fp + om] = npos + ar
                     continue
                 if (h, wid) in promoted:
                     pk, pv = promoted[(h, wid)]
                     nk[h, npos:npos + om] = pk
                     nv[h, npos:npos + om] = pv
                     nl[h, npos:npos + om] = wid
+                    span = find_logical_window_span(self.lid, om, h, wid, S)
+                    if span is not None:
+                        mp[h, span[0]:span[1]] = npos + ar
                 else:
                     span = find_logical_window_span(self.lid, om, h, wid, S)
                     if span is not None:
                         s0, e0 = span
                         nk[h, npos:npos + om] = K[h, s0:e0]
                         nv[h, npos:npos + om] = V[h, s0:e0]
+                        mp[h, s0:e0] = npos + ar
                     nl[h, npos:npos + om] = wid
         if self.dyn_local > 0:
             ols = S - self.dyn_local
@@ -509,6 +524,8 @@ class OracleStickyLayer:
             nv[:, nls:nls + act] = V[:, ols:ols + act]
             lsw = max(0, (self.n_tokens - sink - self.dyn_local) // om)
             nl[:, nls:nls + act] = (lsw + np.arange(self.dyn_local) // om)[:act][None, :]
+            mp[:, ols:ols + act] = (nls + np.arange(act, dtype=np.float32))[None, :]
+        self.last_mapping = mp
         return nk, nv, nl
 
     def decode(self, K, V, scores, q_scores, score_dt):
@@ -561,6 +578,7 @@ class OracleStickyLayer:
         promoted = self.get_promoted_windows(res["winner_ids"])
         self.rebuild(res["loser_ids"], res["loser_scores"], K, V, res["pre_block_wids"], S)
         nk, nv, nl = self.build_physical_cache(K, V, res, promoted)
+        self.last_cycle_votes = self.votes[:, :S].copy()   # what the token ledger sees (cache.py:422-424)
         self.window_scores[:] = np.nan
         self.window_scores[:, :ck, 0] = res["winner_scores"]
         self.window_scores[:, :ck, 1] = res["winner_ids"]

@@ -51,7 +51,7 @@ def lib():
             "`python -c 'import qevict_b200.build as b; b.build()'` (nvcc, sm_100a)")
     L = ctypes.CDLL(_LIB_PATH)
     P = ctypes.POINTER
-    vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+    vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
     D, Lp = P(QvDims), P(QvLayer)
     sig = {
         "qv_ring_windows": (i32, [D]),
@@ -77,6 +77,9 @@ def lib():
         "qv_silu_mul": (ctypes.c_int, [i32, i32, vp, vp, vp]),
         "qv_argmax_workspace_bytes": (sz, [i32]),
         "qv_argmax": (ctypes.c_int, [i32, i32, vp, vp, vp, sz, vp]),
+        "qv_track_prefill": (ctypes.c_int, [i32, i32, i32, i32, i32, i64, i32, vp, i32, vp, i32, vp, vp, vp]),
+        "qv_track_decode": (ctypes.c_int, [i32, i32, i64, i64, i32, i32, vp, i32, vp, vp, vp]),
+        "qv_track_positions": (ctypes.c_int, [i32, i32, i64, i32, vp, vp, i32, vp, vp, vp]),
         "qv_read_error": (ctypes.c_int, [Lp, P(i32), vp]),
         "qv_last_cuda_error": (ctypes.c_char_p, []),
         "qv_version": (ctypes.c_char_p, []),
@@ -97,7 +100,9 @@ def exported_symbols():
             "qv_decode_attention_noalloc", "qv_evict_cycle",
             "qv_evict_cycle_count", "qv_evict_cycle_ext",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
-            "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_argmax_workspace_bytes", "qv_argmax", "qv_read_error",
+            "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul",
+            "qv_argmax_workspace_bytes", "qv_argmax", "qv_track_prefill", "qv_track_decode",
+            "qv_track_positions", "qv_read_error",
             "qv_last_cuda_error", "qv_version"]
 
 

@@ -18,6 +18,13 @@ written against the reference's cache object keeps working:
     ascending id, then the local zone and the tokens appended since.
   * the ``q_cache_*`` / ``window_scores`` / ``global_token_counter`` properties
     present the device state in the reference's shapes and order.
+  * with ``sticky_config.tracking_flag == 1`` the research token ledger
+    (``qevict_b200.tracking.TrackingManager``, one per sequence) is kept on the
+    device exactly as the reference's cache drives it (cache.py:251-260,
+    346-351, 371-373, 414-424); ``token_ledger``, ``global_score_history``,
+    ``prefill_attention_matrix`` and ``get_ledger_data()`` expose it.  The
+    old -> new position mapping of a cycle comes from the token each physical
+    position holds before and after the cycle.
 
 This caller-computes-attention path exists for compatibility; the fused path,
 where the attention kernel computes and folds the probabilities itself, is
@@ -37,6 +44,7 @@ from . import codec as _codec
 from . import sticky_config
 from .allocator import compute_budget
 from .layer_state import StickyLayerState, kv_dtype_code
+from .tracking import NoOpTrackingManager, TrackingManager
 
 
 class STICKYKVCache_LayerWise:
@@ -73,6 +81,10 @@ class STICKYKVCache_LayerWise:
             self.max_windows = max(mw, 100)
         else:
             self.max_windows = 30000
+        # research token ledger (cache.py:112-119,148-153,183-186)
+        self._tracking_flag = getattr(sticky_config, "tracking_flag", 0) == 1
+        self.max_context = max_context if max_context is not None else 131072
+        self.tracking_managers = []
         self.k_windows = 0
         self.local_num = 0
         self.q_windows_count = 0
@@ -91,6 +103,8 @@ class STICKYKVCache_LayerWise:
         self._prefill_done = False
         self._bypass = False
         self._new_tokens = 0
+        for tr in self.tracking_managers:
+            tr.reset()
 
     def attach_workspace(self, workspace):
         """Share one decode/cycle workspace between the layers of a model (one stream)."""
@@ -138,6 +152,10 @@ class STICKYKVCache_LayerWise:
             return past_key_values
         K, V = past_key_values
         if not self._prefill_done:
+            ql = q_len if q_len is not None else attn_score_cache.shape[2]
+            self._trackers(K.shape[0], K.device)
+            for tr in self.tracking_managers:      # counter restarts at a prompt (cache.py:253-257)
+                tr.set_counter(ql)
             if self.total_cache_ratio >= 100 and self.q_ratio == 0:
                 # full cache requested: the prompt KV is kept untouched (cache.py:289-297)
                 self._prefill_done = True
@@ -145,13 +163,29 @@ class STICKYKVCache_LayerWise:
                 return past_key_values
             sc = attn_score_cache
             colsum = sc[:, :, 0, :] if sc.dim() == 4 else sc
-            self.prefill_state(K.contiguous(), V.contiguous(), colsum.contiguous())
+            st = self.prefill_state(K.contiguous(), V.contiguous(), colsum.contiguous())
+            S = K.shape[2]
+            for b, tr in enumerate(self.tracking_managers):   # cache.py:346-351
+                tr.record_prefill(seq_len=S, q_len=ql, layer_idx=self.layer_idx,
+                                  attn_score_cache=attn_score_cache[b:b + 1],
+                                  survivor_ids=st.reference_token_ids(b), full_attn_scores=(
+                                      None if full_attn_scores is None else full_attn_scores[b:b + 1]),
+                                  global_start=0, num_new_tokens=ql)
             return self._physical()
+        gstart = [int(tr.global_token_counter) for tr in self.tracking_managers]
+        for tr in self.tracking_managers:
+            tr.increment(1)
         if self._bypass:
             return past_key_values
-        return self._decode_with_scores(K, V, attn_score_cache, q_attn_scores)
+        return self._decode_with_scores(K, V, attn_score_cache, q_attn_scores, gstart)
 
-    def _decode_with_scores(self, K, V, scores, q_scores):
+    def _trackers(self, B, device):
+        if len(self.tracking_managers) != B:
+            mk = (lambda: TrackingManager(self.max_context, self.num_heads, device)) if self._tracking_flag \
+                else (lambda: NoOpTrackingManager(device))
+            self.tracking_managers = [mk() for _ in range(B)]
+
+    def _decode_with_scores(self, K, V, scores, q_scores, gstart=None):
         """One decode token whose attention the caller computed (cache.py:357-427)."""
         st = self.state
         B, H = st.B, st.H
@@ -181,9 +215,30 @@ class STICKYKVCache_LayerWise:
                 per_win = win.double().sum(dim=2).to(q_scores.dtype).float()
                 o = st.q_order[b, :, :qc[b]].long()
                 st.q_score[b].scatter_add_(1, o, per_win)
+        track = self._tracking_flag and gstart is not None
+        if track:
+            for b, tr in enumerate(self.tracking_managers):   # cache.py:371-373
+                tr.record_decode(scores[b:b + 1], n_ref + 1, self.layer_idx, gstart[b])
         if st.cycle_due():
+            if track:
+                old = [(st.reference_token_ids(b), torch.gather(st.votes[b], 1, st.reference_positions(b)))
+                       for b in range(B)]
             st.evict_cycle()
+            if track:                                          # cache.py:414-424
+                for b, tr in enumerate(self.tracking_managers):
+                    tr.update_physical_positions(self._cycle_mapping(b, old[b][0]), n_ref + 1, old[b][1])
         return self._physical()
+
+    def _cycle_mapping(self, b, old_ids):
+        """[H, S_old] float32: the new physical position of the token each old
+        position held, -1 where that token left the cache (cache.py:456-573)."""
+        st = self.state
+        new_ids = st.reference_token_ids(b)
+        n = int(max(int(old_ids.max()), int(new_ids.max()))) + 1
+        inv = torch.full((st.H, n), -1.0, dtype=torch.float32, device=st.device)
+        pos = torch.arange(new_ids.shape[1], dtype=torch.float32, device=st.device)
+        inv.scatter_(1, new_ids, pos[None].expand(st.H, -1).contiguous())
+        return torch.gather(inv, 1, old_ids).contiguous()
 
     def _physical(self):
         st = self.state
@@ -258,13 +313,31 @@ class STICKYKVCache_LayerWise:
         n = self.state.n_tokens if self.state is not None else self._new_tokens
         return torch.tensor(n, dtype=torch.long)
 
+    def _tracked(self, fn):
+        if not self.tracking_managers:
+            return None
+        vals = [fn(tr) for tr in self.tracking_managers]
+        return vals[0] if len(vals) == 1 else vals
+
+    @property
+    def tracking_manager(self):
+        return self._tracked(lambda tr: tr)
+
     @property
     def token_ledger(self):
-        """The research token-tracking ledger is not kept on the device path."""
-        return None
+        """[max_context, 2 + 2H] float32 token ledger (a list of them when B > 1)."""
+        return self._tracked(lambda tr: tr.token_ledger)
+
+    @property
+    def global_score_history(self):
+        return self._tracked(lambda tr: tr._global_score_history)
+
+    @property
+    def prefill_attention_matrix(self):
+        return self._tracked(lambda tr: tr.prefill_attention_matrix)
 
     def get_ledger_data(self):
-        return None
+        return self._tracked(lambda tr: tr.get_ledger_data())
 
     # -- codec (reference static methods, cache.py:201-228,603-636) ------------------------
     @staticmethod

@@ -223,6 +223,19 @@ class StickyLayerState:
         sinks = torch.arange(sink, device=dev)
         return torch.cat([sinks[None].expand(self.H, -1), sticky, ring[None].expand(self.H, -1)], dim=1)
 
+    def reference_token_ids(self, b):
+        """Token index [H, S_ref] (int64, on the device) held at each position of
+        the reference's physical order, the positions of reference_positions(b):
+        sinks, the tokens of the sticky windows by ascending id, the local zone."""
+        ck = self.counts()[0][b]
+        om, sink, dev = self.omega, self.sink, self.device
+        order = self.sticky_order[b, :, :ck].long()
+        wid = torch.gather(self.sticky_wid[b], 1, order).long()
+        sticky = (sink + wid[:, :, None] * om + torch.arange(om, device=dev)).reshape(self.H, -1)
+        ring = torch.arange(self.last_compaction - self.local, self.n_tokens, device=dev)
+        sinks = torch.arange(sink, device=dev)
+        return torch.cat([sinks[None].expand(self.H, -1), sticky, ring[None].expand(self.H, -1)], dim=1)
+
     def view_kv(self, b):
         """Physical cache in the reference's order: (K [H, S_ref, D], V) as float32 on CPU."""
         pos = self.reference_positions(b)

@@ -20,4 +20,5 @@ R_RATIO = 20                # total cache budget as % of (prompt + max_new_token
 Q_RATIO = 10                # % of the window budget given to the quantised Q-cache
 QUANTIZATION_BIT_WIDTH = 8  # 8 (INT8) or 4 (packed INT4)
 S_IDX = 0                   # start index for window tracking (start_idx)
+tracking_flag = 0           # 1: keep the research token ledger (TrackingManager)
 GENERATION_CONFIG = {"max_new_tokens": 512, "do_sample": False, "temperature": 1.0}

@@ -152,12 +152,22 @@ def gen_attention():
 # 3. cache state machine driven with explicit scores (forced churn)
 # ---------------------------------------------------------------------------
 def gen_state(name, dt, attn_kind, seed, H=2, D=16, omega=16, sink=8, local=32,
-              k_windows=3, q_windows=4, prompt=200, steps=96, bits=8):
+              k_windows=3, q_windows=4, prompt=200, steps=96, bits=8, tracking=False):
     configure(omega, sink, local, k_windows, q_windows, bits)
     cfg = make_config(hidden=4 * D, heads=4, kv_heads=H)
     from src.models.kv_cache.cache import STICKYKVCache_LayerWise
+    # the research token ledger is on when sticky_config.tracking_flag == 1 (cache.py:112-119)
+    sticky_config.tracking_flag = 1 if tracking else 0
     cache = STICKYKVCache_LayerWise(p_ratio=50, r_ratio=20, start_idx=0, num_heads=H,
                                     layer_idx=1, config=cfg)
+    sticky_config.tracking_flag = 0
+    rows = prompt + steps + 8
+
+    def track(rec, p):
+        if tracking:
+            rec[p + "trk_ledger"] = cache.token_ledger[:rows].numpy().copy()
+            rec[p + "trk_hist"] = cache.global_score_history[:rows].numpy().copy()
+            rec[p + "trk_counter"] = np.array(int(cache.global_token_counter))
     td = TD[dt]
     g = torch.Generator().manual_seed(seed)
     K = torch.randn(1, H, prompt, D, generator=g).to(td)
@@ -175,6 +185,7 @@ def gen_state(name, dt, attn_kind, seed, H=2, D=16, omega=16, sink=8, local=32,
                                                    prompt, steps, bits, cache.eviction_manager.window_scores.shape[1]]))
     kv = cache((K, V), attn, q_len=prompt)
     rec["pre_K"], rec["pre_V"] = f32(kv[0]), f32(kv[1])
+    track(rec, "pre_")
     ws0 = cache.window_scores[:, :, 0]
     big = float(torch.nan_to_num(ws0, nan=0.0).max())
     rec["pre_ws"] = cache.window_scores.numpy().copy()
@@ -234,11 +245,13 @@ def gen_state(name, dt, attn_kind, seed, H=2, D=16, omega=16, sink=8, local=32,
                 rec[p + "qks"], rec[p + "qkz"] = f32(cache.q_cache_k_scale), f32(cache.q_cache_k_zp)
                 rec[p + "qvs"], rec[p + "qvz"] = f32(cache.q_cache_v_scale), f32(cache.q_cache_v_zp)
             rec[p + "meta"] = np.array(sorted([list(k) for k in cache.quantization_manager.q_retired_meta.keys()]) or np.zeros((0, 2)), dtype=np.int64)
+            track(rec, p)
             cyc += 1
     rec["newk"], rec["newv"] = np.stack(newk), np.stack(newv)
     rec["scores"], rec["qscores"], rec["qscores_n"] = np.stack(scs), np.stack(qss), np.array(qsn)
     rec["n_cycles"] = np.array(cyc)
     rec["final_K"], rec["final_V"] = f32(kv[0]), f32(kv[1])
+    track(rec, "final_")
     save(name, **rec)
 
 
@@ -325,6 +338,64 @@ def gen_budget():
     save("budget", inputs=np.array(rows, np.int64), outputs=np.array(outs, np.int64))
 
 
+# ---------------------------------------------------------------------------
+# 7. research token ledger, operation by operation (tracking_manager.py:27-204)
+# ---------------------------------------------------------------------------
+def gen_tracking_ops(H=3, C=64, prompt=40, keep=28, steps=30, cycles=(10, 20), layer_idx=5):
+    """TrackingManager driven directly, with the edge cases its callers can
+    produce: score rows shorter than the physical cache (positions out of
+    range), evicted tokens (votes added once more), and a ledger smaller than
+    the token count (rows past max_context are dropped)."""
+    from src.models.kv_cache.tracking_manager import TrackingManager
+    g = torch.Generator().manual_seed(41)
+    tm = TrackingManager(C, H, torch.device("cpu"))
+    rec = {"params": np.array([H, C, prompt, keep, steps, layer_idx])}
+    snaps_l, snaps_h = [], []
+
+    def snap():
+        snaps_l.append(tm.token_ledger.numpy().copy())
+        snaps_h.append(tm._global_score_history.numpy().copy())
+
+    attn = torch.rand(1, H, 1, prompt, generator=g) * 5.0
+    surv = torch.stack([torch.sort(torch.randperm(prompt, generator=g)[:keep]).values for _ in range(H)])
+    tm.increment(n=prompt)
+    tm.record_prefill(seq_len=prompt, q_len=prompt, layer_idx=layer_idx, attn_score_cache=attn,
+                      survivor_ids=surv, full_attn_scores=None, global_start=0, num_new_tokens=prompt)
+    snap()
+    rec["attn"], rec["surv"] = f32(attn), surv.numpy()
+    phys_len = keep
+    scs, kvs, lens, maps, votes = [], [], [], [], []
+    for step in range(steps):
+        gs = int(tm.global_token_counter)
+        tm.increment(n=1)
+        phys_len += 1
+        kv = phys_len - 2 if step % 7 == 3 else phys_len
+        sc = torch.rand(1, H, 1, kv, generator=g)
+        tm.record_decode(sc, phys_len, layer_idx, gs)
+        snap()
+        scs.append(np.pad(f32(sc)[0, :, 0], ((0, 0), (0, 128 - kv))))
+        kvs.append(kv)
+        lens.append(phys_len)
+        if step in cycles:
+            kept = torch.rand(H, phys_len, generator=g) < 0.7
+            mp = torch.full((H, phys_len), -1.0)
+            n_new = int(kept.sum(dim=1).min())
+            for h in range(H):
+                idx = torch.nonzero(kept[h]).flatten()[:n_new]
+                mp[h, idx] = torch.randperm(n_new, generator=g).float()
+            vt = torch.rand(H, C, generator=g) * 3.0
+            tm.update_physical_positions(mp, phys_len, vt)
+            snap()
+            maps.append(np.pad(mp.numpy(), ((0, 0), (0, 128 - phys_len)), constant_values=-1.0))
+            votes.append(vt.numpy())
+            phys_len = n_new
+    rec["scores"], rec["kv"], rec["seq_len"] = np.stack(scs), np.array(kvs), np.array(lens)
+    rec["cycles"], rec["mapping"], rec["votes"] = np.array(cycles), np.stack(maps), np.stack(votes)
+    rec["ledger"], rec["hist"] = np.stack(snaps_l), np.stack(snaps_h)
+    rec["counter"] = np.array(int(tm.global_token_counter))
+    save("tracking_ops", **rec)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     gen_codec()
@@ -336,3 +407,5 @@ if __name__ == "__main__":
     gen_module("module_bf16", "bf16", seed=22)
     gen_prefill()
     gen_budget()
+    gen_state("tracking_fp32_fa", "fp32", "fa", seed=31, tracking=True)
+    gen_tracking_ops()

@@ -191,3 +191,69 @@ def test_prefill_lane(dt):
     np.testing.assert_allclose(out, z[p + "out"][0], atol=atol, rtol=0)
     out2, _ = sdpa_causal_attention(q, k, v, dt)
     np.testing.assert_allclose(out2, z[p + "out"][0], atol=atol / 4 if dt != "fp32" else atol, rtol=0)
+
+
+# ----------------------------------------------------------------------------- token ledger
+def _ledger_eq(tr, ledger, hist, what):
+    R = ledger.shape[0]
+    np.testing.assert_array_equal(tr.ledger[:R], ledger, err_msg=what)
+    np.testing.assert_array_equal(tr.history[:R], hist, err_msg=what)
+    assert (tr.ledger[R:] == -1).all() and (tr.history[R:] == -1).all(), what
+
+
+def test_tracking_ops_replay():
+    """TrackingManager operation by operation: every ledger and history
+    snapshot bit for bit (float32 adds in the reference's order)."""
+    from oracle.tracking import OracleTracker
+    z = load("tracking_ops")
+    H, C, prompt, keep, steps, layer = (int(v) for v in z["params"])
+    tr = OracleTracker(C, H)
+    tr.increment(prompt)
+    tr.record_prefill(prompt, prompt, layer, z["attn"], z["surv"], None, 0, prompt)
+    k = 0
+    _ledger_eq(tr, z["ledger"][k], z["hist"][k], "prefill")
+    cycles = list(z["cycles"])
+    for step in range(steps):
+        gs = tr.counter
+        tr.increment(1)
+        kv, S = int(z["kv"][step]), int(z["seq_len"][step])
+        tr.record_decode(z["scores"][step][None, :, None, :kv], S, layer, gs)
+        k += 1
+        _ledger_eq(tr, z["ledger"][k], z["hist"][k], f"decode {step}")
+        if step in cycles:
+            ci = cycles.index(step)
+            tr.update_physical_positions(z["mapping"][ci][:, :S], S, z["votes"][ci])
+            k += 1
+            _ledger_eq(tr, z["ledger"][k], z["hist"][k], f"positions {step}")
+    assert tr.counter == int(z["counter"]) and k + 1 == z["ledger"].shape[0]
+
+
+def test_tracking_state_replay():
+    """The cache object with tracking on (prefill + 96 decode steps with churn):
+    the oracle's old->new position mapping and ledger reproduce the
+    reference's token ledger and score history bit for bit at every cycle."""
+    from oracle.tracking import OracleTracker, tracked_decode, tracked_prefill
+    z = load("tracking_fp32_fa")
+    H, D, om, sink, local, kw, qw, prompt, steps, bits, maxW = [int(v) for v in z["params"]]
+    dt = str(z["dt"])
+    st = OracleStickyLayer(H, D, om, sink, local, kw, qw, dt, bits, max_windows=maxW,
+                           max_context=4096, window_sum="sequential")
+    tr = OracleTracker(4096, H)
+    K, V = tracked_prefill(st, tr, z["K0"][0], z["V0"][0], z["attn"][0], str(z["attn_dt"]), 1)
+    _ledger_eq(tr, z["pre_trk_ledger"], z["pre_trk_hist"], "prefill")
+    cyc = 0
+    for step in range(steps):
+        Kc = np.concatenate([K, z["newk"][step][:, None]], axis=1)
+        Vc = np.concatenate([V, z["newv"][step][:, None]], axis=1)
+        S = Kc.shape[1]
+        qn = int(z["qscores_n"][step])
+        qs = z["qscores"][step][:, :qn] if qn >= 0 else None
+        K, V = tracked_decode(st, tr, Kc, Vc, z["scores"][step][:, :S], qs, dt, 1)
+        if st.tokens_since == 0:
+            p = f"c{cyc}_"
+            np.testing.assert_array_equal(K, z[p + "K"][0])
+            _ledger_eq(tr, z[p + "trk_ledger"], z[p + "trk_hist"], p)
+            assert tr.counter == int(z[p + "trk_counter"])
+            cyc += 1
+    assert cyc == int(z["n_cycles"]) and cyc >= 5
+    _ledger_eq(tr, z["final_trk_ledger"], z["final_trk_hist"], "final")
