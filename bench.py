@@ -243,10 +243,11 @@ def run_ours(args):
     del ids
 
     W, K = args.warmup, args.steps
-    # per layer: rope_append_kernel, decode_mma_kernel, decode_combine_kernel,
-    # add_rmsnorm_kernel x2, silu_mul_kernel; per step: the first add_rmsnorm_kernel
-    # and argmax_kernel
-    launches_per_step = 6 * model.s.layers + 2
+    # per layer: gemv_kernel x4 (qkv, output, gate/up, down), rope_append_kernel,
+    # decode_mma_kernel, decode_combine_kernel, add_rmsnorm_kernel x2,
+    # silu_mul_kernel; per step: the first add_rmsnorm_kernel, the LM head's
+    # gemv_kernel and argmax_kernel
+    launches_per_step = 10 * model.s.layers + 3
     # warm-up: eager first (allocator / cuBLAS), then graph capture, then graph replays
     n_eager = min(3, W)
     for _ in range(n_eager):

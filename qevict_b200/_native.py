@@ -75,6 +75,7 @@ def lib():
         "qv_dequantize": (ctypes.c_int, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
         "qv_add_rmsnorm": (ctypes.c_int, [i32, i32, vp, vp, vp, ctypes.c_float, vp, vp]),
         "qv_silu_mul": (ctypes.c_int, [i32, i32, vp, vp, vp]),
+        "qv_gemv": (ctypes.c_int, [i32, i32, i32, vp, vp, vp, vp]),
         "qv_argmax_workspace_bytes": (sz, [i32]),
         "qv_argmax": (ctypes.c_int, [i32, i32, vp, vp, vp, sz, vp]),
         "qv_track_prefill": (ctypes.c_int, [i32, i32, i32, i32, i32, i64, i32, vp, i32, vp, i32, vp, vp, vp]),
@@ -100,7 +101,7 @@ def exported_symbols():
             "qv_decode_attention_noalloc", "qv_evict_cycle",
             "qv_evict_cycle_count", "qv_evict_cycle_ext",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
-            "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul",
+            "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_gemv",
             "qv_argmax_workspace_bytes", "qv_argmax", "qv_track_prefill", "qv_track_decode",
             "qv_track_positions", "qv_read_error",
             "qv_last_cuda_error", "qv_version"]

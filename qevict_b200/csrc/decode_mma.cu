@@ -955,6 +955,9 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, 
     __shared__ float sm[MM_CMB_SMEM];
     // wait for the streaming kernel (programmatic dependent launch)
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // a programmatic dependent (the output projection) may start streaming
+    // its weights; it waits for this grid before reading the output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int N0 = L.step[0] - 1;
     combine_unit<DT>(g, L, out, partial, logits, P, N0, blockIdx.y, blockIdx.x, gridDim.x, blocks_per_chunk, sm,
                      threadIdx.x, blockDim.x, BlockSync{});

@@ -32,6 +32,9 @@ __global__ void __launch_bounds__(MO_THREADS) add_rmsnorm_kernel(int K, __nv_bfl
                                                                  const __nv_bfloat16* __restrict__ w, float eps,
                                                                  __nv_bfloat16* __restrict__ h) {
     __shared__ float red[MO_THREADS / 32];
+    // the next projection (launched as a programmatic dependent) may start
+    // streaming its weights now; it waits for this grid before reading h
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int b = blockIdx.x;
     uint4* xr = reinterpret_cast<uint4*>(x + (size_t)b * K);
     const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)b * K) : nullptr;
@@ -90,6 +93,7 @@ __global__ void __launch_bounds__(MO_THREADS) add_rmsnorm_kernel(int K, __nv_bfl
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(int F, int rows, const __nv_bfloat16* __restrict__ gu,
                                                        __nv_bfloat16* __restrict__ out) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int n8 = F / 8;
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * n8) return;

@@ -2,9 +2,11 @@
 
 Used for the full-model decode workload (Llama-3-8B shape: 32 layers, hidden
 4096, 32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256).  A decode
-step per layer: cuBLAS projections into preallocated buffers, with the
-elementwise work between them fused (qv_add_rmsnorm: residual add + the next
-RMSNorm; qv_silu_mul: the MLP activation); attention runs the sm_100a
+step per layer: the projections are weight-streaming GEMVs (qv_gemv, each
+launched as a programmatic dependent so its weight stream starts while the
+kernel before it drains) into preallocated buffers, with the elementwise work
+between them fused (qv_add_rmsnorm: residual add + the next RMSNorm;
+qv_silu_mul: the MLP activation); attention runs the sm_100a
 kernels: RoPE + append, fused decode attention with the ledger fold, and the
 eviction cycle every omega tokens; the LM head's greedy token comes from one
 argmax kernel (qv_argmax).  The prefill (prompt) path is torch/cuBLAS
@@ -184,25 +186,31 @@ class StickyLlamaDecoder:
                                     self.s.rms_eps, N.ptr(self.h), torch.cuda.current_stream(self.device).cuda_stream)
         N.check(rc, "qv_add_rmsnorm")
 
+    def _gemv(self, w, x, y):
+        """y = x @ w.T for the decode rows (qv_gemv: weight-streaming GEMV)."""
+        rc = N.lib().qv_gemv(self.B, w.shape[0], w.shape[1], N.ptr(w), N.ptr(x), N.ptr(y),
+                             torch.cuda.current_stream(self.device).cuda_stream)
+        N.check(rc, "qv_gemv")
+
     def _layer_step(self, li):
         """One decoder layer on self.x; expects self.h = RMSNorm(x) * ln1 and leaves
         self.h = RMSNorm(x_out) * (the next layer's ln1, or the final norm)."""
         s, L, st = self.s, self.layers[li], self.states[li]
         B = self.B
         Hq, H, D = s.heads, s.kv_heads, s.head_dim
-        torch.mm(self.h, L["wqkv"].t(), out=self.qkv)
+        self._gemv(L["wqkv"], self.h, self.qkv)
         q = self.qkv[:, :Hq * D].view(B, Hq, D)
         k = self.qkv[:, Hq * D:(Hq + H) * D].view(B, H, D)
         v = self.qkv[:, (Hq + H) * D:].view(B, H, D)
         qr = st.append(q, k, v, self.cos, self.sin)
         st.attend(qr, self.attn_out)
-        torch.mm(self.attn_out.view(B, Hq * D), L["wo"].t(), out=self.proj)
+        self._gemv(L["wo"], self.attn_out, self.proj)
         self._add_norm(self.proj, L["ln2"])
-        torch.mm(self.h, L["wgu"].t(), out=self.gu)
+        self._gemv(L["wgu"], self.h, self.gu)
         rc = N.lib().qv_silu_mul(B, s.ffn, N.ptr(self.gu), N.ptr(self.act),
                                  torch.cuda.current_stream(self.device).cuda_stream)
         N.check(rc, "qv_silu_mul")
-        torch.mm(self.act, L["wd"].t(), out=self.proj)
+        self._gemv(L["wd"], self.act, self.proj)
         nxt = self.layers[li + 1]["ln1"] if li + 1 < s.layers else self.norm
         self._add_norm(self.proj, nxt)
 
@@ -213,7 +221,7 @@ class StickyLlamaDecoder:
             self._layer_step(li)
             if cycle:
                 self.states[li].evict_cycle()
-        torch.mm(self.h, self.lm_head.t(), out=self.logits)
+        self._gemv(self.lm_head, self.h, self.logits)
         rc = N.lib().qv_argmax(self.B, self.s.vocab, N.ptr(self.logits), N.ptr(self.next_tok), N.ptr(self.argmax_ws),
                                self.argmax_ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
         N.check(rc, "qv_argmax")

@@ -88,3 +88,19 @@ def test_argmax(rows, cols):
         assert torch.equal(out, torch.argmax(x.float(), dim=1))
         assert int(out[0]) == cols // 3
 
+
+
+@pytest.mark.parametrize("rows,n,k", [(1, 4096, 4096), (1, 6144, 4096), (1, 4096, 14336), (3, 1000, 1000),
+                                      (8, 257, 2048), (1, 30000, 4096)])
+def test_gemv(rows, n, k):
+    """qv_gemv against an fp32 reference: fp32 accumulation, one bf16 rounding."""
+    g = torch.Generator(device="cuda").manual_seed(n + k)
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    x = torch.randn(rows, k, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+    rc = N.lib().qv_gemv(rows, n, k, N.ptr(w), N.ptr(x), N.ptr(y), torch.cuda.current_stream().cuda_stream)
+    N.check(rc, "qv_gemv")
+    ref = x.double() @ w.double().t()
+    # one bf16 rounding (2^-8 relative) plus fp32 summation-order error
+    tol = 2.0 ** -8 * ref.abs() + 1e-5 * (x.double().abs() @ w.double().abs().t())
+    assert ((y.double() - ref).abs() <= tol).all()
