@@ -344,6 +344,29 @@ def run_ours(args):
                 if ln.startswith("bytes_per_launch"):
                     traffic = int(ln.split("=")[1])
 
+    # ---- the whole step against HBM: bytes a decode step must read (every
+    # weight once + the live KV of every layer) / device time per step
+    wbytes = sum(L[k].numel() * L[k].element_size() for L in model.layers for k in ("wqkv", "wo", "wgu", "wd"))
+    wbytes += model.lm_head.numel() * model.lm_head.element_size() + model.s.hidden * 2
+    kvbytes = model.s.layers * model.attention_bytes_per_layer((model.k.omega + 1) / 2)
+    step_gbs = (wbytes + kvbytes) / (ms / K * 1e-3) / 1e9
+
+    # ---- decode-attention microbenchmark at batch 64 (one Llama-3-8B layer, 64 sink
+    # + 512 local + 2048 sticky bf16 tokens and 4096 INT8 Q-cache tokens per
+    # sequence, eviction cycle every 64 steps, L2 flushed before every step)
+    attn_b64 = None
+    if rank == 0:
+        try:
+            from qevict_b200 import microbench
+            r = microbench.run(batch=64, steps=200, warmup=8, quiet=True)
+            attn_b64 = {"batch": 64, "steps": 200, "avg_launch_us": r["avg_attention_us"],
+                        "bytes_per_launch": r["avg_bytes_per_launch"], "achieved": r["attention_GBps"],
+                        "unit": "GB/s", "peak": peak, "frac": r["attention_GBps"] / peak,
+                        "cycle_fraction_of_step": r["cycle_fraction_of_step"], "cycle_us_avg": r["cycle_us_avg"],
+                        "l2": "flushed before every step"}
+        except Exception as exc:   # the headline line must still print
+            attn_b64 = {"error": str(exc)[:200]}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -358,6 +381,10 @@ def run_ours(args):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_kind, "traffic": traffic,
                          "avg_launch_us": avg_dur * 1e6, "bytes_per_launch": sum(bytes_) / len(bytes_)},
+            "step_roofline": {"bound": "hbm", "bytes_per_step": wbytes + kvbytes, "weight_bytes": wbytes,
+                              "kv_bytes": kvbytes, "achieved": step_gbs, "peak": peak, "unit": "GB/s",
+                              "frac": step_gbs / peak},
+            "attention_microbench": attn_b64,
             "e2e": e2e,
             "gpu_launches": gpu_launches,
             "clocks": clk.summary(),

@@ -85,6 +85,26 @@ inline cudaError_t ensure_smem(K kernel, size_t bytes, int* cached) {
 int set_cuda_error(cudaError_t e);
 int check_launch();
 
+// Launch as a programmatic dependent of the preceding kernel in the stream:
+// the grid may be scheduled once every CTA of that kernel has executed
+// griddepcontrol.launch_dependents, and must execute griddepcontrol.wait
+// before it reads anything that kernel writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 size_t elt_size(int dt);
 __host__ __device__ constexpr size_t elt_size_dev(int dt) { return dt == QV_F32 ? 4 : 2; }
 

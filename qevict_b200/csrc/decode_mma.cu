@@ -35,8 +35,16 @@
 
 namespace qv {
 
-constexpr int MM_CW = 8;                       // consumer warps
-constexpr int MM_THREADS = (MM_CW + 1) * 32;   // + one producer warp
+// Consumer warps per CTA: MM_CW_WIDE when a CTA holds many items (more warps
+// in flight hide the per-warp latency of the MMA / conversion chains: 2.6 %
+// faster at the batch-64 microbenchmark than 8 warps), MM_CW_NARROW when it
+// holds few (small batch; as many warps as items).
+#ifndef QV_MM_CW_WIDE
+#define QV_MM_CW_WIDE 10
+#endif
+constexpr int MM_CW_NARROW = 8;
+constexpr int MM_CW_WIDE = QV_MM_CW_WIDE;
+static_assert(MM_CW_WIDE >= MM_CW_NARROW && MM_CW_WIDE <= 12, "consumer warps");
 constexpr int MM_STAGE = 17408;                // bytes per stage (17 KB, 1024-aligned)
 constexpr int MM_MAXNS = 12;                   // max pipeline stages
 constexpr int MM_G = 8;                        // max GQA group
@@ -51,6 +59,7 @@ struct MmPlan {
     int nC;           // CTAs (<= total, so every CTA owns at least one item)
     int pmax;         // partial slots per (b, h, zone)
     int ns;           // pipeline stages
+    int cw;           // consumer warps per CTA
 };
 
 __host__ __device__ inline int mm_cta_of(const MmPlan& P, long long i) {
@@ -123,7 +132,8 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return (uint32_t)(row * 128 + (((chunk ^ (row & 7)) & 7) << 4));
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+template <int CW>
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory"); }
 
 // x / sqrt(128) correctly rounded in fp32: product with the rounded reciprocal,
 // then one fused correction with the exact residual (Markstein's method).
@@ -379,8 +389,8 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
 struct BlockSync {
     __device__ void operator()() const { __syncthreads(); }
 };
-template <int DT>
-__global__ void __launch_bounds__(MM_THREADS, 1)
+template <int DT, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
 decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ CUtensorMap tmKQ, const __grid_constant__ CUtensorMap tmVQ,
                   Geo g, qv_layer L, const void* __restrict__ q, int* tickets, float* partial,
@@ -396,9 +406,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     unsigned char* stages = smem;
     // per-warp segment states, double-buffered by segment parity
     float* s_wo = reinterpret_cast<float*>(smem + NS * MM_STAGE);       // [2][CW][G][128]
-    float* s_wm = s_wo + 2 * MM_CW * G * 128;                           // [2][CW][8]
-    float* s_wl = s_wm + 2 * MM_CW * MM_G;                              // [2][CW][8]
-    int* s_cnt = reinterpret_cast<int*>(s_wl + 2 * MM_CW * MM_G);       // [2] arrivals, [2] merges done
+    float* s_wm = s_wo + 2 * CW * G * 128;                           // [2][CW][8]
+    float* s_wl = s_wm + 2 * CW * MM_G;                              // [2][CW][8]
+    int* s_cnt = reinterpret_cast<int*>(s_wl + 2 * CW * MM_G);       // [2] arrivals, [2] merges done
     uint64_t* full = reinterpret_cast<uint64_t*>(s_cnt + 4);
     uint64_t* empty = full + MM_MAXNS;
     unsigned char* s_skip = reinterpret_cast<unsigned char*>(empty + MM_MAXNS);
@@ -436,7 +446,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     const int j_new = (g.ring_base() + (cw % g.R) * 64 + tv - 1) / MM_MT;
 
     // --------------------------------------------------------------- producer
-    if (warp == MM_CW) {
+    if (warp == CW) {
         if (lane == 0 && i0 < i1) {
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
@@ -565,14 +575,14 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 svz[col] += __shfl_xor_sync(0xffffffffu, svz[col], off);
             }
         }
-        float* wo = s_wo + ((size_t)p * MM_CW + warp) * G * 128;
+        float* wo = s_wo + ((size_t)p * CW + warp) * G * 128;
 #pragma unroll
         for (int col = 0; col < 2; ++col) {
             const int hh = 2 * t4 + col;
             if (hh < G) {
                 if (gq == 0) {
-                    s_wm[(p * MM_CW + warp) * MM_G + hh] = m[col];
-                    s_wl[(p * MM_CW + warp) * MM_G + hh] = ls[col];
+                    s_wm[(p * CW + warp) * MM_G + hh] = m[col];
+                    s_wl[(p * CW + warp) * MM_G + hh] = ls[col];
                 }
 #pragma unroll
                 for (int dt = 0; dt < 8; ++dt) {
@@ -591,21 +601,21 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         if (final_seg) {
             // the CTA's last segment: every warp is here, so merge with all threads
-            consumer_sync();
+            consumer_sync<CW>();
             int first, cnt;
             mm_zone_ctas(P, bh, zone, &first, &cnt);
             float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
-            const float* wm = s_wm + p * MM_CW * MM_G;
-            const float* wl = s_wl + p * MM_CW * MM_G;
-            const float* wo0 = s_wo + (size_t)p * MM_CW * G * 128;
-            for (int idx = threadIdx.x; idx < G * 128; idx += MM_CW * 32) {
+            const float* wm = s_wm + p * CW * MM_G;
+            const float* wl = s_wl + p * CW * MM_G;
+            const float* wo0 = s_wo + (size_t)p * CW * G * 128;
+            for (int idx = threadIdx.x; idx < G * 128; idx += CW * 32) {
                 const int hh = idx >> 7, d = idx & 127;
                 float M = -INFINITY;
 #pragma unroll
-                for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
+                for (int w = 0; w < CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
                 float acc = 0.f, lsum = 0.f;
 #pragma unroll
-                for (int w = 0; w < MM_CW; ++w) {
+                for (int w = 0; w < CW; ++w) {
                     const float mw = wm[w * MM_G + hh];
                     if (mw == -INFINITY) continue;
                     const float ew = __expf(mw - M);
@@ -621,24 +631,24 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         __threadfence_block();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(s_cnt + p, 1) == MM_CW - 1;
+        if (lane == 0) last = atomicAdd(s_cnt + p, 1) == CW - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
             __threadfence_block();
             int first, cnt;
             mm_zone_ctas(P, bh, zone, &first, &cnt);
             float* part = partial + (((size_t)bh * 2 + zone) * P.pmax + (c - first)) * G * 130;
-            const float* wm = s_wm + p * MM_CW * MM_G;
-            const float* wl = s_wl + p * MM_CW * MM_G;
-            const float* wo0 = s_wo + (size_t)p * MM_CW * G * 128;
+            const float* wm = s_wm + p * CW * MM_G;
+            const float* wl = s_wl + p * CW * MM_G;
+            const float* wo0 = s_wo + (size_t)p * CW * G * 128;
             for (int hh = 0; hh < G; ++hh) {
                 float M = -INFINITY;
 #pragma unroll
-                for (int w = 0; w < MM_CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
-                float ew[MM_CW];
+                for (int w = 0; w < CW; ++w) M = fmaxf(M, wm[w * MM_G + hh]);
+                float ew[CW];
                 float lsum = 0.f;
 #pragma unroll
-                for (int w = 0; w < MM_CW; ++w) {
+                for (int w = 0; w < CW; ++w) {
                     const float mw = wm[w * MM_G + hh];
                     ew[w] = mw == -INFINITY ? 0.f : __expf(mw - M);
                     lsum += wl[w * MM_G + hh] * ew[w];
@@ -647,7 +657,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 for (int d = lane; d < 128; d += 32) {
                     float acc = 0.f;
 #pragma unroll
-                    for (int w = 0; w < MM_CW; ++w)
+                    for (int w = 0; w < CW; ++w)
                         if (ew[w] != 0.f) acc += wo0[((size_t)w * G + hh) * 128 + d] * ew[w];
                     part[hh * 130 + 2 + d] = acc;
                 }
@@ -714,7 +724,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         if (skipped(i)) continue;
         const int kk_item = k++;
-        if (kk_item % MM_CW != warp) continue;   // another warp's item
+        if (kk_item % CW != warp) continue;   // another warp's item
         const int s = kk_item % NS;
         // A warp that gives up waiting keeps walking the items (and joins every
         // named barrier) without computing, so no barrier is left unmatched.
@@ -931,12 +941,14 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         if (lane == 0) mbar_arrive(&empty[s]);
     }
     // let the combine grid get scheduled while this grid drains (it waits for
-    // this grid's completion before reading anything)
+    // this grid's completion before reading anything).  Triggering at the
+    // start instead, with fewer stages at batch 1 so that a combine block fits
+    // beside each CTA, was measured: 0.08 ms slower per 32-layer decode step.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // every CTA has read the token counter at its start; the last one to finish
     // advances it (the combine kernel reads the advanced value)
     __threadfence();
-    consumer_sync();
+    consumer_sync<CW>();
     if (threadIdx.x == 0) {
         if (atomicAdd(tickets, 1) == (int)gridDim.x - 1) {
             tickets[0] = 0;
@@ -1004,8 +1016,8 @@ bool mm_supported(const Geo& g) {
            g.om == 64 && g.sink % 64 == 0 && g.bits == 8 && g.G <= MM_G && g.S_cap % 64 == 0;
 }
 
-static size_t mm_fixed_smem(const Geo& g) {
-    return 1024 + (size_t)(2 * MM_CW * g.G * 128 + 4 * MM_CW * MM_G) * 4 + 16 + 2 * MM_MAXNS * 8 + MM_SKIPMAP;
+static size_t mm_fixed_smem(const Geo& g, int cw) {
+    return 1024 + (size_t)(2 * cw * g.G * 128 + 4 * cw * MM_G) * 4 + 16 + 2 * MM_MAXNS * 8 + MM_SKIPMAP;
 }
 
 MmPlan mm_plan(const Geo& g) {
@@ -1019,7 +1031,10 @@ MmPlan mm_plan(const Geo& g) {
     P.nC = (int)(nc < 1 ? 1 : nc);
     const long long wz = P.n_main > P.n_q ? P.n_main : P.n_q;
     P.pmax = (int)((wz * P.nC + P.total - 1) / P.total + 2);
-    int ns = (int)((232448 - mm_fixed_smem(g)) / MM_STAGE);
+    // items of the fullest CTA: with many per CTA more consumer warps hide latency
+    const long long per_cta = (P.total + P.nC - 1) / P.nC;
+    P.cw = per_cta >= 2 * MM_CW_WIDE ? MM_CW_WIDE : MM_CW_NARROW;
+    const int ns = (int)((232448 - mm_fixed_smem(g, P.cw)) / MM_STAGE);
     P.ns = ns > MM_MAXNS ? MM_MAXNS : ns;
     return P;
 }
@@ -1039,7 +1054,7 @@ size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
 int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s) {
     MmPlan P = mm_plan(g);
     // a consumer warp may wait on a stage only one fill ahead of it: stages >= warps
-    if (P.pmax > 64 || P.ns < MM_CW) return QV_EINVAL;
+    if (P.pmax > 64 || P.ns < P.cw) return QV_EINVAL;
     size_t op, ol;
     mm_ws_bytes(g, &op, &ol);
     char* base = reinterpret_cast<char*>(ws);
@@ -1053,8 +1068,8 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     okm = okm && make_map(&mkq, kqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64) &&
           make_map(&mvq, vqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64);
     if (!okm) return QV_EINVAL;
-    const size_t smem = mm_fixed_smem(g) + (size_t)P.ns * MM_STAGE;
-    static int cached[3] = {48 * 1024, 48 * 1024, 48 * 1024};
+    const size_t smem = mm_fixed_smem(g, P.cw) + (size_t)P.ns * MM_STAGE;
+    static int cached[2][2] = {{48 * 1024, 48 * 1024}, {48 * 1024, 48 * 1024}};
     int* tickets = reinterpret_cast<int*>(base);
     float* part = reinterpret_cast<float*>(base + op);
     void* lgt = base + ol;
@@ -1071,7 +1086,7 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg1 = {};
     cfg1.gridDim = dim3(P.nC);
-    cfg1.blockDim = dim3(MM_THREADS);
+    cfg1.blockDim = dim3((P.cw + 1) * 32);
     cfg1.dynamicSmemBytes = smem;
     cfg1.stream = s;
     cfg1.attrs = attr;
@@ -1080,9 +1095,11 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     cfg2.gridDim = dim3(chunks, BH);
     cfg2.blockDim = dim3(256);
     cfg2.dynamicSmemBytes = 0;
-    auto kern = g.dt == QV_BF16 ? decode_mma_kernel<QV_BF16> : decode_mma_kernel<QV_F16>;
+    const bool wide = P.cw == MM_CW_WIDE;
+    auto kern = g.dt == QV_BF16 ? (wide ? decode_mma_kernel<QV_BF16, MM_CW_WIDE> : decode_mma_kernel<QV_BF16, MM_CW_NARROW>)
+                                : (wide ? decode_mma_kernel<QV_F16, MM_CW_WIDE> : decode_mma_kernel<QV_F16, MM_CW_NARROW>);
     auto comb = g.dt == QV_BF16 ? decode_combine_kernel<QV_BF16> : decode_combine_kernel<QV_F16>;
-    cudaError_t e = ensure_smem(kern, smem, &cached[g.dt == QV_BF16 ? 1 : 2]);
+    cudaError_t e = ensure_smem(kern, smem, &cached[g.dt == QV_BF16 ? 0 : 1][wide ? 1 : 0]);
     if (e != cudaSuccess) return set_cuda_error(e);
     e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
     if (e != cudaSuccess) return set_cuda_error(e);

@@ -1,26 +1,36 @@
 // Weight-streaming GEMV of the full-model decode driver: y[b] = W . x[b] for
 // a bf16 nn.Linear weight W [N][K] (row-major) and a handful of token rows x.
 //
-// At decode batch 1-8 a projection is a pure HBM stream of W, so the kernel is
-// built around keeping enough of W in flight:
-//   * one warp per output row at a time, 16-byte loads (8 weights per lane),
-//     groups of U loads per lane (U KiB per warp) double-buffered in
-//     registers, so the next group is in flight while the current one is
-//     multiplied;
-//   * a persistent grid sized by occupancy; each warp walks its rows and its
-//     groups as one stream, so the loads of the next row start before the
-//     current row is reduced.  U = 2 when the resident warps cover every row
-//     at once (one row per warp, the smallest registers), else U = 4 (more
-//     bytes in flight per warp); measured on B200 against cuBLAS back to back
-//     at the Llama-3-8B projection shapes: qkv 11.7 vs 15.6 us, output
-//     9.2 vs 15.4, gate/up 38.7 vs 42.1, down 26.0 vs 29.1, LM head 152 vs 163;
-//   * weights bypass L1 (read once); x (tiny, shared by every warp) is read
-//     through L1;
-//   * programmatic dependent launch: W does not depend on the preceding
-//     kernel, so each warp issues its first group before griddepcontrol.wait
-//     and the stream starts while the preceding kernel drains.
-// fp32 accumulation, one rounding to bf16 per output (as a bf16 GEMM with
-// fp32 compute rounds).
+// At decode batch 1-8 a projection is a pure HBM stream of W.  Two layouts of
+// the work, chosen by the row length:
+//
+// Rows (K <= 8192): one warp per output row at a time, 16-byte loads (8
+// weights per lane), groups of U loads per lane (U KiB per warp)
+// double-buffered in registers, so the next group is in flight while the
+// current one is multiplied; a persistent grid sized by occupancy; each warp
+// walks its rows and its groups as one stream, so the loads of the next row
+// start before the current row is reduced.  U = 2 when the resident warps
+// cover every row at once (one row per warp, the smallest registers), else
+// U = 4 (more bytes in flight per warp).  Measured on B200 against cuBLAS back
+// to back at the Llama-3-8B projection shapes: qkv 11.7 vs 15.6 us, output
+// 9.2 vs 15.4, gate/up 38.7 vs 42.1, LM head 152 vs 163.
+//
+// K-slices (K > 8192, the MLP down projection): with rows of 28 KiB and only
+// N = 4096 of them, one row per warp leaves the SMs unevenly loaded (3-4 CTAs
+// each) and too few bytes in flight.  Instead each CTA (8 warps, as many per
+// SM as fit) owns an equal contiguous range of rows, warp w takes K-slice w of
+// every one of them, and the eight partial dot products of a row meet in
+// shared memory and are added in warp order; loads are grouped U at a time
+// and double-buffered like the row layout (a group is consumed as a whole, so
+// its loads share one scoreboard).  Down projection: 23.7 us vs 26.1 for the
+// row layout.
+//
+// Both: weights bypass L1 (read once; an L2 evict-first policy on them was
+// measured: no gain); x (tiny, shared by every warp) is read through L1; the
+// kernel is a programmatic dependent of the one before it, issues its first
+// weight loads before griddepcontrol.wait (W does not depend on that kernel)
+// and reads x after it.  fp32 accumulation, one rounding to bf16 per output
+// (as a bf16 GEMM with fp32 compute rounds).
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -29,7 +39,10 @@
 namespace qv {
 
 constexpr int GV_THREADS = 256;
+constexpr int GV_WARPS = GV_THREADS / 32;
 constexpr int GV_MAXB = 8;              // token rows
+constexpr int GV_PASS = 32;             // K-slices: rows whose partials are held in shared memory at a time
+constexpr int GV_KSPLIT_MIN_K = 8192;   // K above which the K-slice layout is used
 
 __device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
     uint4 v;
@@ -41,8 +54,9 @@ __device__ __forceinline__ uint4 ld_stream16(const uint4* p) {
 __device__ __forceinline__ float gv_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float gv_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
+// Row layout (see the top of this file).
 template <int NB, int GV_U>
-__global__ void __launch_bounds__(GV_THREADS) gemv_kernel(int N, int K, const __nv_bfloat16* __restrict__ W,
+__global__ void __launch_bounds__(GV_THREADS) gemv_rows_kernel(int N, int K, const __nv_bfloat16* __restrict__ W,
                                                           const __nv_bfloat16* __restrict__ x,
                                                           __nv_bfloat16* __restrict__ y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,6 +126,104 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(int N, int K, const __
     }
 }
 
+// K-slice layout (see the top of this file).  CTA c owns rows
+// [c*N/grid, (c+1)*N/grid); warp w of the CTA owns chunks [w*cs, (w+1)*cs) of
+// each of them.
+template <int NB, int U>
+__global__ void __launch_bounds__(GV_THREADS, NB <= 2 ? 4 : 2)
+gemv_ksplit_kernel(int N, int K, const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restrict__ x,
+                   __nv_bfloat16* __restrict__ y) {
+    __shared__ float part[GV_PASS][GV_WARPS][NB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nc = K >> 3;                                   // 16-byte chunks per row
+    const int cs = (nc + GV_WARPS - 1) / GV_WARPS;           // chunks of this warp's slice
+    const int cpl = (cs + 31) >> 5;                          // chunks per lane per row slice
+    const int c_lo = warp * cs;
+    const int c_hi = min(c_lo + cs, nc);
+    const int row0 = (int)((long long)blockIdx.x * N / gridDim.x);
+    const int nrows = (int)((long long)(blockIdx.x + 1) * N / gridDim.x) - row0;
+    // this warp's chunks, in order: row r = 0..nrows-1, then i = 0..cpl-1 within
+    // the row's slice (chunk c_lo + lane + 32 i); loaded U at a time into one of
+    // two register buffers, each buffer consumed as a whole (so a buffer's loads
+    // share one scoreboard and the two buffers alternate)
+    const int n_groups = (nrows * cpl + U - 1) / U;
+    const uint4* __restrict__ wbase = reinterpret_cast<const uint4*>(W) + (size_t)row0 * nc;
+    int lr = 0, li = 0;                                      // load cursor: row, chunk of the slice
+    auto load_group = [&](uint4* buf) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int c = c_lo + lane + 32 * li;
+            buf[u] = (lr < nrows && c < c_hi) ? ld_stream16(wbase + (size_t)lr * nc + c) : make_uint4(0u, 0u, 0u, 0u);
+            if (++li == cpl) { li = 0; ++lr; }
+        }
+    };
+    uint4 bufA[U], bufB[U];
+    load_group(bufA);
+    // x is written by the preceding kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    const uint4* __restrict__ xg = reinterpret_cast<const uint4*>(x);
+    float acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+    int cr = 0, ci = 0, pr = 0;                              // consume cursor: row, chunk, row in pass
+    auto consume_group = [&](const uint4* buf) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (cr < nrows) {
+                const int c = c_lo + lane + 32 * ci;
+                if (c < c_hi) {
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(&buf[u]);
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) {
+                        const uint4 xv = __ldg(xg + (size_t)b * nc + c);
+                        const uint32_t* xp = reinterpret_cast<const uint32_t*>(&xv);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            acc[b] = fmaf(gv_lo(wp[q]), gv_lo(xp[q]), acc[b]);
+                            acc[b] = fmaf(gv_hi(wp[q]), gv_hi(xp[q]), acc[b]);
+                        }
+                    }
+                }
+                if (++ci == cpl) {              // this warp's slice of row cr is complete
+                    ci = 0;
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) {
+                        const float sum = warp_sum(acc[b]);
+                        if (lane == 0) part[pr][warp][b] = sum;
+                        acc[b] = 0.f;
+                    }
+                    // every warp reaches the end of a pass at the same point:
+                    // add the slices of the pass's rows in warp order and store
+                    if (++pr == GV_PASS || cr == nrows - 1) {
+                        __syncthreads();
+                        const int rp = cr + 1 - pr;     // first row of the pass
+                        for (int i = threadIdx.x; i < pr * NB; i += GV_THREADS) {
+                            const int rr = i / NB, b = i % NB;
+                            float sum = 0.f;
+#pragma unroll
+                            for (int w2 = 0; w2 < GV_WARPS; ++w2) sum += part[rr][w2][b];
+                            y[(size_t)b * N + row0 + rp + rr] = __float2bfloat16_rn(sum);
+                        }
+                        __syncthreads();
+                        pr = 0;
+                    }
+                    ++cr;
+                }
+            }
+        }
+    };
+#pragma unroll 1
+    for (int g = 0; g < n_groups; g += 2) {
+        load_group(bufB);
+        consume_group(bufA);
+        if (g + 1 >= n_groups) break;
+        load_group(bufA);
+        consume_group(bufB);
+    }
+}
+
 static int gv_sms() {
     static int n = 0;
     if (n == 0) {
@@ -122,37 +234,40 @@ static int gv_sms() {
     return n;
 }
 
-template <int NB, int U>
-static cudaError_t gemv_launch_u(int N, int K, const void* w, const void* x, void* y, cudaStream_t s, int per_sm) {
-    const long long need = ((long long)N + GV_THREADS / 32 - 1) / (GV_THREADS / 32);
-    const long long cap = (long long)per_sm * gv_sms();
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(need < cap ? need : cap));
-    cfg.blockDim = dim3(GV_THREADS);
-    cfg.stream = s;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NB, U>, N, K, static_cast<const __nv_bfloat16*>(w),
-                              static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y));
+template <typename Kern>
+static cudaError_t gv_launch(Kern kern, unsigned grid, int N, int K, const void* w, const void* x, void* y,
+                             cudaStream_t s) {
+    return launch_pdl(kern, dim3(grid), dim3(GV_THREADS), 0, s, N, K, static_cast<const __nv_bfloat16*>(w),
+                      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y));
+}
+
+static int gv_resident(const void* kern) {
+    int per = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, GV_THREADS, 0) != cudaSuccess || per < 1) per = 1;
+    return per;
 }
 
 template <int NB>
 static cudaError_t gemv_launch(int N, int K, const void* w, const void* x, void* y, cudaStream_t s) {
+    if (K > GV_KSPLIT_MIN_K) {
+        constexpr int U = NB <= 2 ? 4 : 2;
+        static int per = 0;
+        if (per == 0) per = gv_resident((const void*)gemv_ksplit_kernel<NB, U>);
+        const long long cap = (long long)per * gv_sms();
+        return gv_launch(gemv_ksplit_kernel<NB, U>, (unsigned)(N < cap ? N : cap), N, K, w, x, y, s);
+    }
     static int per2 = 0, per4 = 0;
     if (per2 == 0) {
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per2, gemv_kernel<NB, 2>, GV_THREADS, 0) != cudaSuccess ||
-            per2 < 1)
-            per2 = 1;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per4, gemv_kernel<NB, 4>, GV_THREADS, 0) != cudaSuccess ||
-            per4 < 1)
-            per4 = 1;
+        per2 = gv_resident((const void*)gemv_rows_kernel<NB, 2>);
+        per4 = gv_resident((const void*)gemv_rows_kernel<NB, 4>);
     }
-    if ((long long)N <= (long long)per2 * gv_sms() * (GV_THREADS / 32))
-        return gemv_launch_u<NB, 2>(N, K, w, x, y, s, per2);
-    return gemv_launch_u<NB, 4>(N, K, w, x, y, s, per4);
+    const long long need = ((long long)N + GV_WARPS - 1) / GV_WARPS;
+    if ((long long)N <= (long long)per2 * gv_sms() * GV_WARPS) {
+        const long long cap = (long long)per2 * gv_sms();
+        return gv_launch(gemv_rows_kernel<NB, 2>, (unsigned)(need < cap ? need : cap), N, K, w, x, y, s);
+    }
+    const long long cap = (long long)per4 * gv_sms();
+    return gv_launch(gemv_rows_kernel<NB, 4>, (unsigned)(need < cap ? need : cap), N, K, w, x, y, s);
 }
 
 }  // namespace qv

@@ -91,7 +91,9 @@ def test_argmax(rows, cols):
 
 
 @pytest.mark.parametrize("rows,n,k", [(1, 4096, 4096), (1, 6144, 4096), (1, 4096, 14336), (3, 1000, 1000),
-                                      (8, 257, 2048), (1, 30000, 4096)])
+                                      (8, 257, 2048), (1, 30000, 4096),
+                                      # K > 8192: the K-slice layout (ragged slices, several token rows)
+                                      (2, 4096, 14336), (3, 1000, 8200), (8, 300, 16384), (1, 7, 9000)])
 def test_gemv(rows, n, k):
     """qv_gemv against an fp32 reference: fp32 accumulation, one bf16 rounding."""
     g = torch.Generator(device="cuda").manual_seed(n + k)
