@@ -11,7 +11,8 @@
 //     with 2-D TMA tiles (128-byte swizzle, no multicast) and 1-D bulk copies for
 //     the Q-cache scales; every mbarrier wait is bounded.  Items holding no live
 //     token (empty sticky / Q slots) are never fetched.
-//   * Eight consumer warps each take whole items, round-robin, and run both
+//   * Eight (or, for CTAs with many items, ten) consumer warps each take whole
+//     items, round-robin, and run both
 //     products on the tensor cores with the GQA group in the MMA's N dimension:
 //     S^T[tok, head] = K[tok, :] . Q^T  and  O^T[d, head] += V^T[d, tok] . P^T,
 //     P^T obtained from the S^T accumulators by movmatrix.  BF16 P is split into
