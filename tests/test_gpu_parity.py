@@ -92,7 +92,8 @@ def _check_state(st, oracles, Kref, Vref, where):
 
 
 def run_parity(dt, bits=8, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3, qw=4,
-               n_prompt_windows=10, steps=256, seed=0, churn=True, maxW=64, reference_rounding=False):
+               n_prompt_windows=10, steps=256, seed=0, churn=True, maxW=64, reference_rounding=False,
+               max_context=4096):
     """Prefill + decode + eviction cycles on the GPU and in the oracle, step by step.
 
     The tensor-core decode path dequantises the Q-cache exactly (code*scale + zp
@@ -114,7 +115,7 @@ def run_parity(dt, bits=8, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3
     oracles, Kref, Vref = [], [], []
     for b in range(B):
         o = OracleStickyLayer(H, D, om, sink, local, kw, qw, dt, bits, max_windows=maxW,
-                              max_context=4096, window_sum="tree")
+                              max_context=max_context, window_sum="tree")
         K, V = o.prefill(Kp[b], Vp[b], colsum[b][:, None, :], "fp32")
         oracles.append(o)
         Kref.append(K)
@@ -212,6 +213,17 @@ def test_decode_reference_rounding_mode(dt):
 def test_decode_int4_qcache():
     n, _ = run_parity("bf16", bits=4, steps=128)
     assert n == 2
+
+
+def test_decode_many_items_per_cta():
+    """The full-model layer shape at batch 4: 4 x 8 (sequence, head) pairs of 116
+    items (84 main-zone tiles of 32 tokens + 32 Q windows) = 3712 items over 148
+    CTAs, 26 per CTA -- enough that the tensor-core kernel runs with ten consumer
+    warps instead of eight.  Attention outputs, logits and ledger against the
+    oracle for a few steps (the cycle does not depend on the warp count)."""
+    n, _ = run_parity("bf16", B=4, H=8, local=512, kw=32, qw=32, n_prompt_windows=72, steps=6,
+                      churn=False, maxW=128, max_context=8192)
+    assert n == 0
 
 
 def test_decode_mha_and_small_budget():
