@@ -339,15 +339,15 @@ class STICKYKVCache_LayerWise:
     def get_ledger_data(self):
         return self._tracked(lambda tr: tr.get_ledger_data())
 
-    # -- codec (reference static methods, cache.py:201-228,603-636) ------------------------
+    # -- codec (reference static methods, cache.py:626-637; same parameter names) ----------
     @staticmethod
-    def _quantize_k_per_window(k_data, bit_width=8):
-        return _codec.quantize_k_per_window(k_data, bit_width)
+    def _quantize_k_per_window(tensor, bit_width=8):
+        return _codec.quantize_k_per_window(tensor, bit_width)
 
     @staticmethod
-    def _quantize_v_per_window(v_data, bit_width=8):
-        return _codec.quantize_v_per_window(v_data, bit_width)
+    def _quantize_v_per_window(tensor, bit_width=8):
+        return _codec.quantize_v_per_window(tensor, bit_width)
 
     @staticmethod
-    def _dequantize_from_quant(q, s, z, bit_width=8):
-        return _codec.dequantize_from_quant(q, s, z, bit_width)
+    def _dequantize_from_quant(quant_tensor, scale, zero_point, bit_width=8):
+        return _codec.dequantize_from_quant(quant_tensor, scale, zero_point, bit_width)
