@@ -24,6 +24,9 @@ from .numerics import f32, op, rnd, mean_round
 
 
 def _exact_dequant(codes, scale, zp, bit_width):
+    """code * scale + zp without intermediate rounding (float64): the tensor-core
+    kernel's dequantisation, in place of dequantize_from_quant's per-op rounding
+    to the KV dtype (quantize.py:62-71); INT4 codes unpacked high nibble first."""
     codes = np.asarray(codes)
     if bit_width == 4:
         hi = (codes >> 4) & 0x0F

@@ -17,6 +17,7 @@ from .numerics import f32, op, rnd, to_uint8_like_torch
 
 
 def _levels(bit_width):
+    """Quantisation levels: 255 for INT8, 15 for INT4 (quantize.py:37-53)."""
     return 15.0 if bit_width == 4 else 255.0
 
 

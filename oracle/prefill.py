@@ -19,7 +19,9 @@ from .numerics import f32, mean_round, op, rnd, sum_round
 
 
 def causal_attention(q, k, v, dt):
-    """q [Hq, S, D], k/v [H, S, D] -> out [Hq, S, D] (values in dt)."""
+    """Causal GQA attention of the prompt: q [Hq, S, D], k/v [H, S, D] -> out [Hq, S, D]
+    (values in dt) -- the SDPA prefill of src/models/attention/module.py:258-304 with
+    the causal mask of ops.py:53-67 (FA2 path: ops_flash.py:22-49)."""
     Hq, S, D = q.shape
     H = k.shape[0]
     G = Hq // H

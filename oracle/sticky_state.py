@@ -46,7 +46,9 @@ NEG_INF = np.float32(-np.inf)
 
 
 def topk_desc(scores, k):
-    """Row-wise top-k, values descending, ties broken by lower index (see module doc)."""
+    """Row-wise top-k, values descending, ties broken by lower index (see module doc):
+    the torch.topk(..., largest=True) of eviction_manager.py:329,343 and
+    eviction.py:132,147, whose order among equal scores torch leaves unspecified."""
     scores = f32(scores)
     order = np.argsort(-scores.astype(np.float64), axis=1, kind="stable")[:, :k]
     return np.take_along_axis(scores, order, axis=1), order
@@ -90,7 +92,9 @@ def find_logical_window_span(lid, omega, h, wid, seq_len):
 
 
 class OracleStickyLayer:
-    """Reference-layout Sticky-KV state of one layer for one sequence."""
+    """Reference-layout Sticky-KV state of one layer for one sequence: the state that
+    STICKYKVCache_LayerWise (src/models/kv_cache/cache.py:41-427) keeps through its
+    eviction and quantization managers (eviction_manager.py, quantize_manager.py)."""
 
     def __init__(self, num_heads, head_dim, omega, sink, local_num, k_windows, q_windows,
                  dtype, bit_width=8, max_windows=100, max_context=None, r_ratio=20,
@@ -129,6 +133,7 @@ class OracleStickyLayer:
         self.last_cycle_votes = None  # the vote ledger the last cycle consumed [H, S]
 
     def window_to_token(self, ids):
+        """Token indices of windows ids: sink + id*omega + [0, omega) (eviction.py:26-60)."""
         return self.sink + np.asarray(ids, np.int64)[..., None] * self.omega + np.arange(self.omega)
 
     # -- prefill -----------------------------------------------------------------
@@ -594,6 +599,8 @@ class OracleStickyLayer:
         return self.q
 
     def sticky_ids(self):
+        """(ids, scores) of the tracked sticky windows, ascending id: the non-NaN rows of
+        window_scores (eviction_manager.py:385-396 writes them id-sorted)."""
         ws = self.window_scores
         n = int((~np.isnan(ws[0, :, 1])).sum())
         return ws[:, :n, 1].astype(np.int64), ws[:, :n, 0].copy()
@@ -626,4 +633,5 @@ def apply_rope(x, cos, sin, dt):
 
 
 def sdpa_scale(head_dim):
+    """sqrt(head_dim) as the float32 the logits are divided by (ops.py:40,45,123,126)."""
     return np.float32(math.sqrt(head_dim))

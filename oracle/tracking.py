@@ -16,6 +16,8 @@ from .numerics import f32, sum_round
 
 
 class OracleTracker:
+    """The research token ledger of TrackingManager (src/models/kv_cache/tracking_manager.py:27-204)."""
+
     def __init__(self, max_context, num_heads):
         """tracking_manager.py:30-41."""
         self.H = num_heads
