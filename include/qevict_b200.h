@@ -244,7 +244,8 @@ int qv_add_rmsnorm(int32_t rows, int32_t cols, void* x, const void* delta, const
 int qv_silu_mul(int32_t rows, int32_t cols, const void* gate_up, void* out, qv_stream_t stream);
 /* qv_gemv: y[r] = bf16(W . x[r]) for r < rows (1..8), W [n][k] bf16 row-major
  * (an nn.Linear weight), x [rows][k], y [rows][n]; fp32 accumulation; k a
- * multiple of 8, W and x 16-byte aligned.  Launched as a programmatic
+ * multiple of 8, W and x 16-byte aligned.  The summation order is fixed, so
+ * repeated calls give identical results.  Launched as a programmatic
  * dependent of the preceding kernel (its weight stream starts before that
  * kernel ends; x is read after it). */
 int qv_gemv(int32_t rows, int32_t n, int32_t k, const void* w, const void* x, void* y, qv_stream_t stream);
