@@ -182,7 +182,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    tps, n, per_layer, threads = cpu_oracle_parallel(budget_s=max(10.0, 0.5 * args.steps))
+    # a bounded sample: 10-60 s of decode steps per worker, whatever --steps says
+    tps, n, per_layer, threads = cpu_oracle_parallel(budget_s=min(60.0, max(10.0, 0.5 * args.steps)))
     sample = (f"oracle port (numpy), one independent sequence per host core ({threads} processes), 1 of "
               f"32 layers at the workload's decode state, {n} decode steps in total incl. eviction cycles; "
               f"{per_layer * 1e3:.1f} ms per layer-step, x32 layers")
