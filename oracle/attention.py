@@ -49,6 +49,14 @@ def _logits(q, k, dt, raw=False):
     return (lg, r) if raw else lg
 
 
+def exact_dequant_qcache(qcache, bit_width=8):
+    """(kdq, vdq) float64 [H, W, w, D] of a Q-cache dict, dequantised exactly
+    (code * scale + zp): pass them back in ``qcache`` as "kdq"/"vdq" to skip the
+    work on every step while the Q-cache does not change."""
+    return (_exact_dequant(qcache["kq"], qcache["ks"], qcache["kz"], bit_width),
+            _exact_dequant(qcache["vq"], qcache["vs"], qcache["vz"], bit_width))
+
+
 def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="reference",
                      logits_override=None, return_extras=False):
     """Attention of one decode token.
@@ -64,35 +72,80 @@ def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="r
     q        [Hq, D]  rotated query (values in dt)
     k_main   [H, S, D], v_main [H, S, D] physical main cache incl. the new token
     qcache   None or dict(kq [H,W,w,D] u8, ks [H,W,1,D], kz [H,W,1,D],
-                          vq [H,W,w,D] u8, vs [H,W,w,1], vz [H,W,w,1])
+                          vq [H,W,w,D] u8, vs [H,W,w,1], vz [H,W,w,1]);
+             with dequant="exact" it may also carry "kdq"/"vdq" from
+             exact_dequant_qcache (reused instead of recomputed)
     logits_override: [H, G, S + W*w] rounded logits to use instead of the
         ones computed here (lets a test feed the kernel's own logits through the
         rest of the computation).
     Returns (out [Hq, D] in dt, scores_main [H, S] in dt, scores_q [H, W*w] in dt or None)
     and, with return_extras, a dict with the logits, the raw (pre-rounding) dot
-    products and the bound on |kernel logit - oracle logit| per token.
+    products, the bound on |kernel logit - oracle logit| per token, and the
+    per-element magnitudes a tolerance on the output is derived from:
+      out_ulps  ulp(out_main) + ulp(out_q) + ulp(out): the reference rounds the
+                two zones' products and their sum separately (ops.py:132-150)
+      abs_main  sum_t p_t |v_t| over the main zone   [Hq, D]
+      abs_q     the same over the Q-cache            [Hq, D]
+      abs_exp   sum_t p_t |v_t| (2 + 1.173 |x_t|), x_t = logit_t - max, both
+                zones: the weight of the fast exponential's error, at most
+                (2 + 1.173 |x|) fp32 ulps (CUDA's stated bound for __expf)
     """
     q = f32(q)
     H, S, D = k_main.shape
     G = q.shape[0] // H
     qg = q.reshape(H, G, D)
-    main, raw_main = _logits(qg, f32(k_main), dt, raw=True)  # [H, G, S]
-    absdot = np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)), np.abs(f32(k_main).astype(np.float64)))
-    fold = None
+    kdq = vdq = None
     if qcache is not None:
         if dequant == "exact":
-            kdq = _exact_dequant(qcache["kq"], qcache["ks"], qcache["kz"], bit_width)
-            vdq = _exact_dequant(qcache["vq"], qcache["vs"], qcache["vz"], bit_width)
+            if "kdq" in qcache:
+                kdq, vdq = qcache["kdq"], qcache["vdq"]
+            else:
+                kdq, vdq = exact_dequant_qcache(qcache, bit_width)
         else:
             kdq = dequantize_from_quant(qcache["kq"], qcache["ks"], qcache["kz"], dt, bit_width)
             vdq = dequantize_from_quant(qcache["vq"], qcache["vs"], qcache["vz"], dt, bit_width)
         Hc, W, w, _ = kdq.shape
         kdq = kdq.reshape(H, W * w, D)
         vdq = vdq.reshape(H, W * w, D)
-        ql, raw_q = _logits(qg, kdq, dt, raw=True)
-        all_l = np.concatenate([main, ql], axis=-1)
-        raw = np.concatenate([raw_main, raw_q], axis=-1)
-        absdot = np.concatenate([absdot, np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)), np.abs(kdq))], axis=-1)
+    need_logits = logits_override is None or return_extras
+    if need_logits:
+        main, raw_main = _logits(qg, f32(k_main), dt, raw=True)  # [H, G, S]
+        fold = None
+        if qcache is not None:
+            ql, raw_q = _logits(qg, kdq, dt, raw=True)
+            all_l = np.concatenate([main, ql], axis=-1)
+            raw = np.concatenate([raw_main, raw_q], axis=-1)
+        else:
+            all_l = main
+            raw = raw_main
+    if logits_override is not None:
+        all_l = f32(logits_override)
+    x = all_l.astype(np.float64)
+    m = x.max(axis=-1, keepdims=True)
+    e = np.exp(x - m)
+    p = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+    p = rnd(p, dt)
+    pm = p[..., :S]
+    vm64 = f32(v_main).astype(np.float64)
+    out = rnd(np.einsum("hgs,hsd->hgd", pm.astype(np.float64), vm64), dt)
+    scores_q = None
+    out_main, out_q = out, None
+    if qcache is not None:
+        pq = p[..., S:]
+        vdq64 = np.asarray(vdq, np.float64)
+        out_q = rnd(np.einsum("hgs,hsd->hgd", pq.astype(np.float64), vdq64), dt)
+        out = op(np.add, dt, out, out_q)
+        scores_q = mean_round(pq, 1, dt)
+    scores_main = mean_round(pm, 1, dt)
+    if not return_extras:
+        return out.reshape(H * G, D), scores_main, scores_q
+    # one ulp of the dtype at the rounded dot product, divided by sqrt(D), plus one
+    # ulp at the logit, plus the fp16 scale-folding error of Q-cache tokens
+    sd = math.sqrt(D)
+    absdot = np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)), np.abs(f32(k_main).astype(np.float64)))
+    if qcache is not None:
+        absdot = np.concatenate([absdot, np.einsum("hgd,hsd->hgs", np.abs(qg.astype(np.float64)),
+                                                   np.abs(np.asarray(kdq, np.float64)))], axis=-1)
         if dequant == "exact":
             # the kernel folds the K scale into q and rounds q*scale to fp16
             codes = np.asarray(qcache["kq"])
@@ -103,39 +156,26 @@ def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="r
             # fp32 accumulation of the 1024-offset products inside the MMA
             fold = fold + (np.sum(qs, axis=(3, 4))[..., None] * 1024.0 * 2.0 ** -20)
             fold = fold.reshape(H, G, -1)
-    else:
-        all_l = main
-        raw = raw_main
-    if logits_override is not None:
-        all_l = f32(logits_override)
-    x = all_l.astype(np.float64)
-    m = x.max(axis=-1, keepdims=True)
-    e = np.exp(x - m)
-    p = (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
-    p = rnd(p, dt)
-    pm = p[..., :S]
-    out = rnd(np.einsum("hgs,hsd->hgd", pm.astype(np.float64), f32(v_main).astype(np.float64)), dt)
-    scores_q = None
-    out_main, out_q = out, None
-    if qcache is not None:
-        pq = p[..., S:]
-        out_q = rnd(np.einsum("hgs,hsd->hgd", pq.astype(np.float64), vdq.astype(np.float64)), dt)
-        out = op(np.add, dt, out, out_q)
-        scores_q = mean_round(pq, 1, dt)
-    scores_main = mean_round(pm, 1, dt)
-    if not return_extras:
-        return out.reshape(H * G, D), scores_main, scores_q
-    # one ulp of the dtype at the rounded dot product, divided by sqrt(D), plus one
-    # ulp at the logit, plus the fp16 scale-folding error of Q-cache tokens
-    sd = math.sqrt(D)
     # fp32 accumulation of the D products (any order): at most ~64 u * sum|q_d k_d|
     acc = absdot * 64.0 * 2.0 ** -24
     bound = (_ulp(raw, dt) / sd + _ulp(all_l, dt) + acc / sd) * 1.01
     if fold is not None:
         bound[..., S:] += fold / sd
-    # the reference rounds out_main and out_q separately (ops.py:150): an
-    # implementation whose pre-rounding values differ by a hair can land one
-    # ulp away on either, so outputs are compared with these two ulps added
-    out_ulps = _ulp(out_main, dt) + (_ulp(out_q, dt) if out_q is not None else 0.0)
+    # the reference rounds out_main and out_q separately and then their sum
+    # (ops.py:150): an implementation whose pre-rounding values differ by a
+    # hair can land one ulp away on any of the three
+    out_ulps = _ulp(out_main, dt) + _ulp(out, dt)
+    if out_q is not None:
+        out_ulps = out_ulps + _ulp(out_q, dt)
+    pf = p.astype(np.float64)
+    ex = pf * (2.0 + 1.173 * np.abs(x - m))
+    abs_main = np.einsum("hgs,hsd->hgd", pf[..., :S], np.abs(vm64))
+    abs_exp = np.einsum("hgs,hsd->hgd", ex[..., :S], np.abs(vm64))
+    abs_q = np.zeros_like(abs_main)
+    if qcache is not None:
+        abs_q = np.einsum("hgs,hsd->hgd", pf[..., S:], np.abs(vdq64))
+        abs_exp = abs_exp + np.einsum("hgs,hsd->hgd", ex[..., S:], np.abs(vdq64))
     return out.reshape(H * G, D), scores_main, scores_q, dict(
-        logits=all_l, raw=raw, bound=bound, out_ulps=out_ulps.reshape(H * G, D))
+        logits=all_l, raw=raw, bound=bound, out_ulps=out_ulps.reshape(H * G, D),
+        abs_main=abs_main.reshape(H * G, D), abs_q=abs_q.reshape(H * G, D),
+        abs_exp=abs_exp.reshape(H * G, D))

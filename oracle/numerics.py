@@ -17,13 +17,22 @@ def f32(x):
 
 
 def _bf16_rne(x32):
+    """Round float32 values to the nearest bfloat16 (ties to even), as float32.
+
+    In uint32 arithmetic: add 0x7FFF plus the lowest kept bit, then clear the
+    low 16 bits.  No finite input overflows (the largest, 0xFF7FFFFF + 0x8000,
+    stays below 2^32; infinities map to themselves); NaNs are restored after."""
     x32 = np.ascontiguousarray(x32, dtype=np.float32)
-    u = x32.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
-    out = r.astype(np.uint32).view(np.float32)
+    u = x32.view(np.uint32)
+    r = u >> 16
+    r &= 1
+    r += 0x7FFF
+    r += u
+    r &= 0xFFFF0000
+    out = r.view(np.float32)
     nan = np.isnan(x32)
     if nan.any():
-        out = np.where(nan, np.float32(np.nan), out)
+        out[nan] = np.float32(np.nan)
     return out
 
 

@@ -127,6 +127,10 @@ class OracleStickyLayer:
         self.oob_sticky_drops = 0
         self.oob_qcache_b_drops = 0
         self.oob_qcache_c_drops = 0
+        # how many (head, window) entries each Q-cache rebuild path produced
+        # (quantize_manager.py:168-182 A, :243-268 B, :273-318 C; "_zero": the
+        # window was not found in the old cache and was filled with zeros)
+        self.path_counts = dict(A=0, B=0, B_zero=0, C=0, C_zero=0)
         self.last_result = None
         self.last_survivors = None    # prefill survivor positions [H, N] (eviction.py:225-229)
         self.last_mapping = None      # last cycle's old -> new positions [H, S]
@@ -412,6 +416,7 @@ class OracleStickyLayer:
             old_idx = match.astype(np.uint8).argmax(axis=2)
             for h, j in zip(*np.nonzero(ret)):
                 i = old_idx[h, j]
+                self.path_counts["A"] += 1
                 for dst, src in ((nkq, "kq"), (nvq, "vq"), (nks, "ks"), (nkz, "kz"), (nvs, "vs"), (nvz, "vz")):
                     dst[h, j] = self.q[src][h, i]
         else:
@@ -444,6 +449,8 @@ class OracleStickyLayer:
                     else:
                         kf = np.zeros((om, D), np.float32)
                         vf = np.zeros((om, D), np.float32)
+                        self.path_counts["C_zero"] += 1
+                    self.path_counts["C"] += 1
                     ks, kz, vs, vz = self.meta[(wid, h)]
                     nkq[h, j] = requantize_with_meta(kf[None], ks, kz, dt, self.bits)[0]
                     nvq[h, j] = requantize_with_meta(vf, vs, vz, dt, self.bits)
@@ -453,9 +460,11 @@ class OracleStickyLayer:
                     pos = np.clip(phys[n] + np.arange(om), 0, seq_len - 1)
                     kd = K[h, pos].copy()
                     vd = V[h, pos].copy()
+                    self.path_counts["B"] += 1
                     if not found[n]:
                         kd[:] = 0
                         vd[:] = 0
+                        self.path_counts["B_zero"] += 1
                     kq, ks, kz = quantize_k_per_window(kd[None], dt, self.bits)
                     vq, vs, vz = quantize_v_per_window(vd[None], dt, self.bits)
                     nkq[h, j], nks[h, j], nkz[h, j] = kq[0], ks[0], kz[0]

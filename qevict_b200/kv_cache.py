@@ -93,6 +93,7 @@ class STICKYKVCache_LayerWise:
         self._prefill_done = False
         self._bypass = False
         self._new_tokens = 0
+        self._counter = 0     # global token counter while no device state exists (bypass)
         self._workspace = None
         self.reference_rounding = False
 
@@ -103,6 +104,7 @@ class STICKYKVCache_LayerWise:
         self._prefill_done = False
         self._bypass = False
         self._new_tokens = 0
+        self._counter = 0
         for tr in self.tracking_managers:
             tr.reset()
 
@@ -157,10 +159,18 @@ class STICKYKVCache_LayerWise:
             for tr in self.tracking_managers:      # counter restarts at a prompt (cache.py:253-257)
                 tr.set_counter(ql)
             if self.total_cache_ratio >= 100 and self.q_ratio == 0:
-                # full cache requested: the prompt KV is kept untouched (cache.py:289-297)
+                # full cache requested: the prompt KV is kept untouched (cache.py:302-304)
                 self._prefill_done = True
                 self._bypass = True
+                self._counter = ql
                 return past_key_values
+            if self.total_cache_ratio == 100:
+                # the reference evicts at the prefill and then never compacts again
+                # (cache.py:391-397): its physical cache grows without bound, which
+                # a fixed slot layout cannot hold
+                raise N.QevictError("R_RATIO == 100 with a Q-cache (Q_RATIO > 0) is not supported: the "
+                                    "reference stops compacting after the prefill in that mode; use "
+                                    "Q_RATIO = 0 for the full cache, or R_RATIO != 100")
             sc = attn_score_cache
             colsum = sc[:, :, 0, :] if sc.dim() == 4 else sc
             st = self.prefill_state(K.contiguous(), V.contiguous(), colsum.contiguous())
@@ -176,6 +186,7 @@ class STICKYKVCache_LayerWise:
         for tr in self.tracking_managers:
             tr.increment(1)
         if self._bypass:
+            self._counter += 1
             return past_key_values
         return self._decode_with_scores(K, V, attn_score_cache, q_attn_scores, gstart)
 
@@ -310,7 +321,10 @@ class STICKYKVCache_LayerWise:
 
     @property
     def global_token_counter(self):
-        n = self.state.n_tokens if self.state is not None else self._new_tokens
+        if self.state is not None:
+            n = self.state.n_tokens
+        else:
+            n = self._counter if self._bypass else self._new_tokens
         return torch.tensor(n, dtype=torch.long)
 
     def _tracked(self, fn):

@@ -1,8 +1,9 @@
 """Generate golden vectors by running the reference implementation itself.
 
-Run in a container that has the reference checkout (default
-``/root/reference``, override with QEVICT_REFERENCE).  The reference is
-imported read-only, with the harness patches it needs on current libraries:
+Run where a checkout of the reference is available; its path is the first
+argument or the QEVICT_REFERENCE environment variable (there is no default).
+The reference is imported read-only, with the harness patches it needs on
+current libraries:
 
   * ``sticky_config`` knobs (OMEGA, SINK_TOKENS, QUANTIZATION_BIT_WIDTH,
     LOCAL_NUM_TOKENS) set before construction (read at cache.py:66-119);
@@ -15,7 +16,10 @@ Each scenario records its seeded inputs and the reference's outputs into
 ``tests/golden/<name>.npz``; ``tests/test_oracle_golden.py`` replays the inputs
 through the oracle and compares.  Fixtures are small (sub-MB).
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference checkout> [scenario ...]
+
+Scenarios: codec attention state module prefill budget tracking module_c1
+(default: all but module_c1, which takes about a minute and ~10 GB of RAM).
 """
 
 import os
@@ -23,9 +27,13 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("QEVICT_REFERENCE", "/root/reference")
+_ARGS = [a for a in sys.argv[1:] if not a.startswith("-")]
+REF = _ARGS.pop(0) if _ARGS and os.path.isdir(_ARGS[0]) else os.environ.get("QEVICT_REFERENCE")
+if not REF or not os.path.isdir(REF):
+    sys.exit("usage: make_golden.py <reference checkout> [scenario ...]  (or set QEVICT_REFERENCE)")
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.dont_write_bytecode = True
+sys.path.insert(0, OUT)
 sys.path.insert(0, REF)
 sys.path.insert(0, os.path.join(REF, "src"))
 
@@ -36,6 +44,7 @@ import src.models.kv_cache.cache as ref_cache_mod  # noqa: E402
 from src.models.kv_cache.allocator import BudgetResult  # noqa: E402
 from src.models.kv_cache import quantize as ref_q  # noqa: E402
 from src.models.attention import ops as ref_ops  # noqa: E402
+from c1_inputs import C1, c1_inputs  # noqa: E402
 
 TD = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
 
@@ -396,16 +405,92 @@ def gen_tracking_ops(H=3, C=64, prompt=40, keep=28, steps=30, cycles=(10, 20), l
     save("tracking_ops", **rec)
 
 
+
+
+# ---------------------------------------------------------------------------
+# 8. the single-layer fp32 workload at full shape (one Llama attention layer)
+# ---------------------------------------------------------------------------
+def gen_module_c1(c=C1):
+    """The reference's STICKYLlamaAttention at the fp32 single-layer workload's
+    full shape: 32 query / 8 KV heads, head_dim 128, RoPE theta 500000, a
+    4096-token prompt and 256 decode steps, omega 64, sink 64, local 256, 16
+    sticky + 16 INT8 Q windows (SDPA path, sticky_config.USE_FLASH_ATTENTION=0).
+    Records the prefill output at every 128th position, every decode output's
+    first 1024 elements (and whole-vector sums), the window sets after the
+    prefill and after each of the four eviction cycles, and the final Q-cache
+    scales / zero points and code checksums."""
+    configure(c["omega"], c["sink"], c["local"], c["k_windows"], c["q_windows"], 8)
+    cfg = make_config(hidden=c["hidden"], heads=c["heads"], kv_heads=c["kv_heads"],
+                      max_pos=c["prompt"] + c["steps"] + 64)
+    from src.models.attention.module import STICKYLlamaAttention
+    from transformers import DynamicCache
+    w, hs, dec = c1_inputs(c)
+    m = STICKYLlamaAttention(cfg, 1)
+    with torch.no_grad():
+        for lin, name in ((m.q_proj, "q"), (m.k_proj, "k"), (m.v_proj, "v"), (m.o_proj, "o")):
+            lin.weight.copy_(torch.from_numpy(w[name]))
+    cache = DynamicCache()
+    kc = m.kv_cache
+    em = kc.eviction_manager
+    kw = c["k_windows"]
+
+    def windows():
+        ids = em.window_scores[:, :kw, 1].numpy().copy()
+        qids = kc.q_cache_ids.numpy().copy() if kc.q_cache_ids is not None else np.zeros((0,), np.float32)
+        return ids, qids
+
+    rec = {}
+    with torch.no_grad():
+        o_pre, _ = m(torch.from_numpy(hs)[None], past_key_values=cache, use_cache=True)
+        o_pre = f32(o_pre)[0]
+        rec["pre_rows"] = np.arange(0, c["prompt"], 128)
+        rec["out_pre"] = o_pre[rec["pre_rows"]]
+        rec["out_pre_rowsum"] = o_pre.astype(np.float64).sum(axis=1)
+        ids, qids = windows()
+        sticky, qsets, cyc_steps = [ids], [qids], [-1]
+        outs = []
+        for i in range(c["steps"]):
+            o, _ = m(torch.from_numpy(dec[i])[None, None], past_key_values=cache, use_cache=True)
+            outs.append(f32(o)[0, 0])
+            if em.tokens_since_last_review == 0:
+                ids, qids = windows()
+                sticky.append(ids)
+                qsets.append(qids)
+                cyc_steps.append(i)
+    outs = np.stack(outs)
+    rec["out_dec"] = outs[:, :1024]
+    rec["out_dec_sum"] = outs.astype(np.float64).sum(axis=1)
+    rec["out_dec_abssum"] = np.abs(outs.astype(np.float64)).sum(axis=1)
+    rec["sticky_ids"] = np.stack(sticky)
+    rec["q_ids"] = np.stack(qsets)
+    rec["cycle_steps"] = np.array(cyc_steps)
+    rec["q_ks"], rec["q_kz"] = f32(kc.q_cache_k_scale), f32(kc.q_cache_k_zp)
+    rec["q_vs"], rec["q_vz"] = f32(kc.q_cache_v_scale), f32(kc.q_cache_v_zp)
+    kq, vq = kc.q_cache_k_quant.numpy(), kc.q_cache_v_quant.numpy()
+    rec["q_kq_sum"] = kq.astype(np.int64).sum(axis=(2, 3))
+    rec["q_vq_sum"] = vq.astype(np.int64).sum(axis=(2, 3))
+    rec["q_kq_w0"], rec["q_vq_w0"] = kq[:, 0].copy(), vq[:, 0].copy()
+    rec["global_token_counter"] = np.array(int(kc.global_token_counter))
+    rec["config"] = np.array([c[k] for k in ("hidden", "heads", "kv_heads", "omega", "sink", "local",
+                                             "k_windows", "q_windows", "prompt", "steps", "seed")])
+    save("module_c1_fp32", **rec)
+
+
+SCENARIOS = {
+    "codec": lambda: gen_codec(),
+    "attention": lambda: gen_attention(),
+    "state": lambda: (gen_state("state_bf16_sdpa", "bf16", "sdpa", seed=11),
+                      gen_state("state_fp32_fa", "fp32", "fa", seed=12),
+                      gen_state("state_fp16_fa", "fp16", "fa", seed=13)),
+    "module": lambda: (gen_module("module_fp32", "fp32", seed=21), gen_module("module_bf16", "bf16", seed=22)),
+    "prefill": lambda: gen_prefill(),
+    "budget": lambda: gen_budget(),
+    "tracking": lambda: (gen_state("tracking_fp32_fa", "fp32", "fa", seed=31, tracking=True), gen_tracking_ops()),
+    "module_c1": lambda: gen_module_c1(),
+}
+
+
 if __name__ == "__main__":
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    gen_codec()
-    gen_attention()
-    gen_state("state_bf16_sdpa", "bf16", "sdpa", seed=11)
-    gen_state("state_fp32_fa", "fp32", "fa", seed=12)
-    gen_state("state_fp16_fa", "fp16", "fa", seed=13)
-    gen_module("module_fp32", "fp32", seed=21)
-    gen_module("module_bf16", "bf16", seed=22)
-    gen_prefill()
-    gen_budget()
-    gen_state("tracking_fp32_fa", "fp32", "fa", seed=31, tracking=True)
-    gen_tracking_ops()
+    for name in (_ARGS or [k for k in SCENARIOS if k != "module_c1"]):
+        SCENARIOS[name]()

@@ -53,3 +53,34 @@ def test_invalid_dims_rejected():
     for d in bad:
         assert N.lib().qv_ring_windows(ctypes.byref(d)) == -1
         assert N.lib().qv_main_capacity(ctypes.byref(d)) == -1
+
+
+@pytest.mark.parametrize("name,dims,path", [
+    # the production layer: bf16 / fp16, head_dim 128, omega 64, INT8, sink a multiple of 64
+    ("bf16 int8 omega64", (1, 8, 4, 128, 64, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0), 1),
+    ("fp16 int8 omega64 MHA", (16, 32, 1, 128, 64, 64, 512, 8, 64, 512, 8, N.QV_F16, 0), 1),
+    # everything else takes the CUDA-core kernel
+    ("bf16 INT4", (1, 8, 4, 128, 64, 64, 512, 32, 32, 512, 4, N.QV_BF16, 0), 0),
+    ("bf16 omega 16", (1, 8, 4, 128, 16, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0), 0),
+    ("bf16 omega 32", (1, 8, 4, 128, 32, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0), 0),
+    ("bf16 sink 4", (1, 8, 4, 128, 64, 4, 512, 32, 32, 512, 8, N.QV_BF16, 0), 0),
+    ("bf16 head_dim 64", (1, 8, 4, 64, 64, 64, 512, 32, 32, 512, 8, N.QV_BF16, 0), 0),
+    ("fp32", (1, 8, 4, 128, 64, 64, 512, 32, 32, 512, 8, N.QV_F32, 0), 0),
+    ("bf16 reference rounding", (1, 8, 4, 128, 64, 64, 512, 32, 32, 512, 8, N.QV_BF16,
+                                 N.QV_FLAG_REFERENCE_ROUNDING), 0),
+])
+def test_decode_path_selection(name, dims, path):
+    """Which decode-attention kernel each configuration gets (qv_decode_path is host
+    arithmetic only): 1 = the tensor-core kernel, 0 = the CUDA-core kernel.  A
+    configuration that silently falls back to the slower kernel shows up here."""
+    d = N.QvDims(*dims)
+    assert N.lib().qv_decode_path(ctypes.byref(d)) == path, name
+
+
+def test_reference_default_omega_8_rejected():
+    """The reference's shipped defaults (src/sticky_config.py: OMEGA 8, SINK_TOKENS 4,
+    4-bit codes) are refused: windows must be a multiple of 16 tokens, 16..128
+    (every workload of this library uses omega 64)."""
+    d = N.QvDims(1, 8, 4, 128, 8, 4, 32, 4, 4, 512, 4, N.QV_BF16, 0)
+    assert N.lib().qv_decode_path(ctypes.byref(d)) == -1
+    assert N.lib().qv_main_capacity(ctypes.byref(d)) == -1

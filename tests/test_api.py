@@ -174,3 +174,150 @@ def test_attention_module_matches_oracle(knobs):
         np.testing.assert_array_equal(ids.numpy(), o.window_scores[:, :ids.shape[1], 1])
         assert kc.state.read_error() == 0
         assert int(kc.global_token_counter) == S + steps
+
+
+def _c1_inputs():
+    import importlib.util
+    path = os.path.join(GOLDEN, "c1_inputs.py")
+    spec = importlib.util.spec_from_file_location("c1_inputs", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.C1, mod.c1_inputs
+
+
+@pytest.mark.gpu
+def test_attention_module_c1_matches_reference_golden(knobs, monkeypatch):
+    """STICKYLlamaAttention (fp32) at the single-layer workload's full shape against
+    outputs of the reference's own STICKYLlamaAttention on the same seeded inputs
+    (tests/golden/module_c1_fp32.npz, written by make_golden.py module_c1): a
+    4096-token prompt and 256 decode steps, free running on both sides (each
+    side's own projections, logits, ledger and cycles).  Decode outputs: plain
+    max-abs <= 1e-5; window sets after the prefill and after each of the four
+    cycles: equal; final Q-cache scales within fp32 rounding of the inputs."""
+    torch = _cuda()
+    import qevict_b200.kv_cache as kvmod
+    from qevict_b200.allocator import BudgetResult
+    from qevict_b200.attention import STICKYLlamaAttention
+    C1, c1_inputs = _c1_inputs()
+    z = np.load(os.path.join(GOLDEN, "module_c1_fp32.npz"))
+    assert [int(x) for x in z["config"]] == [C1[k] for k in ("hidden", "heads", "kv_heads", "omega", "sink", "local",
+                                                             "k_windows", "q_windows", "prompt", "steps", "seed")]
+    knobs(OMEGA=C1["omega"], SINK_TOKENS=C1["sink"], LOCAL_NUM_TOKENS=C1["local"], Q_RATIO=10,
+          QUANTIZATION_BIT_WIDTH=8, GENERATION_CONFIG={"max_new_tokens": C1["steps"]})
+    # the same fixed window budget the golden's generator gave the reference
+    monkeypatch.setattr(kvmod, "compute_budget", lambda **kw: BudgetResult(
+        C1["local"], C1["k_windows"], C1["q_windows"], 0, kw.get("head_dim", 0)))
+    old_prec = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        cfg = SimpleNamespace(hidden_size=C1["hidden"], num_attention_heads=C1["heads"],
+                              num_key_value_heads=C1["kv_heads"], max_position_embeddings=C1["prompt"] + C1["steps"] + 64,
+                              rope_theta=500000.0, r_ratio=20, p_ratio=50, start_idx=0)
+        w, hs, dec = c1_inputs(C1)
+        m = STICKYLlamaAttention(cfg, 1).cuda()
+        with torch.no_grad():
+            for lin, name in ((m.q_proj, "q"), (m.k_proj, "k"), (m.v_proj, "v"), (m.o_proj, "o")):
+                lin.weight.copy_(torch.from_numpy(w[name]))
+            out_pre, _ = m(torch.from_numpy(hs).cuda()[None], use_cache=True)
+            out_pre = out_pre[0].double().cpu().numpy()
+            st = m.kv_cache.state
+            kw = C1["k_windows"]
+
+            def windows():
+                ids, _ = st.view_sticky(0)
+                q = st.view_q(0)
+                return ids.numpy().astype(np.float32), q["ids"].numpy()
+
+            pre_err = float(np.abs(out_pre[z["pre_rows"]] - z["out_pre"]).max())
+            sticky, qsets = [], []
+            ids, qids = windows()
+            sticky.append(ids)
+            qsets.append(qids)
+            outs = []
+            for i in range(C1["steps"]):
+                o, _ = m(torch.from_numpy(dec[i]).cuda()[None, None], use_cache=True)
+                outs.append(o[0, 0].double().cpu().numpy())
+                if st.last_compaction == st.n_tokens:
+                    ids, qids = windows()
+                    sticky.append(ids)
+                    qsets.append(qids)
+        outs = np.stack(outs)
+        dec_err = float(np.abs(outs[:, :1024] - z["out_dec"]).max())
+        sum_err = float(np.abs(outs.sum(axis=1) - z["out_dec_sum"]).max())
+        print(f"\n[C1 module vs reference golden] prefill rows max-abs {pre_err:.3e}, decode max-abs {dec_err:.3e}, "
+              f"decode row-sum max-abs {sum_err:.3e}")
+        assert len(sticky) == len(z["sticky_ids"]) == 5
+        for c in range(5):
+            np.testing.assert_array_equal(sticky[c], z["sticky_ids"][c][:, :kw], err_msg=f"sticky ids, cycle {c}")
+            for h in range(C1["kv_heads"]):
+                assert sorted(qsets[c][h].tolist()) == sorted(z["q_ids"][c][h].tolist()), f"Q window set, cycle {c}"
+        order_same = np.mean([np.array_equal(a, b) for a, b in zip(qsets, z["q_ids"])])
+        print(f"[C1] Q-cache top-k order identical after {order_same * 100:.0f} % of the cycles")
+        assert dec_err <= 1e-5, dec_err
+        assert pre_err <= 4e-5, pre_err
+        q = st.view_q(0)
+        # order the final Q windows like the reference's before comparing per window
+        perm = [[list(q["ids"][h].numpy()).index(x) for x in z["q_ids"][-1][h]] for h in range(C1["kv_heads"])]
+        hh = np.arange(C1["kv_heads"])[:, None]
+        for key, ref in (("ks", z["q_ks"]), ("kz", z["q_kz"]), ("vs", z["q_vs"]), ("vz", z["q_vz"])):
+            np.testing.assert_allclose(q[key].numpy()[hh, perm], ref, rtol=1e-5, atol=1e-6, err_msg=key)
+        ksum = q["kq"].numpy().astype(np.int64).sum(axis=(2, 3))[hh, perm]
+        vsum = q["vq"].numpy().astype(np.int64).sum(axis=(2, 3))[hh, perm]
+        # a code can sit on a rounding boundary of (x - zp) / scale: at most a
+        # handful of +-1 flips per window of 8192 codes
+        assert np.abs(ksum - z["q_kq_sum"]).max() <= 16 and np.abs(vsum - z["q_vq_sum"]).max() <= 16
+        assert int(m.kv_cache.global_token_counter) == int(z["global_token_counter"])
+        assert st.read_error() == 0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_prec
+
+
+def test_full_cache_bypass_r_ratio_100(knobs):
+    """R_RATIO >= 100 with Q_RATIO == 0 keeps the prompt KV untouched and never
+    evicts (cache.py:302-304: the prefill returns past_key_values as given;
+    the decode branch then returns early, as logical_id_map stays None,
+    cache.py:364-365); the counter still advances.  The oracle's state after
+    its own prefill at R_RATIO 100 / no Q-cache is the same identity.  No
+    device state is built, so this runs on the host."""
+    import torch
+    from qevict_b200.kv_cache import STICKYKVCache_LayerWise
+    H, G, D, om, sink, local = 2, 2, 64, 16, 16, 32
+    knobs(OMEGA=om, SINK_TOKENS=sink, LOCAL_NUM_TOKENS=local, Q_RATIO=0, QUANTIZATION_BIT_WIDTH=8,
+          GENERATION_CONFIG={"max_new_tokens": 40})
+    cfg = SimpleNamespace(hidden_size=H * G * D, num_attention_heads=H * G, num_key_value_heads=H,
+                          max_position_embeddings=1024)
+    cache = STICKYKVCache_LayerWise(50, 100, 0, H, 1, cfg)
+    dev = torch.device("cpu")
+    S = sink + 7 * om + 5          # any length: nothing is cut into windows
+    K = torch.randn(1, H, S, D, device=dev)
+    V = torch.randn(1, H, S, D, device=dev)
+    cs = torch.rand(1, H, 1, S, device=dev)
+    Kg, Vg = cache((K, V), cs, q_len=S)
+    assert Kg is K and Vg is V
+    assert cache.state is None
+    for i in range(2 * om + 3):
+        K = torch.cat([K, torch.randn(1, H, 1, D, device=dev)], 2)
+        V = torch.cat([V, torch.randn(1, H, 1, D, device=dev)], 2)
+        sc = torch.rand(1, H, 1, K.shape[2], device=dev)
+        Kg, Vg = cache((K, V), sc, q_len=1)
+        assert Kg is K and Vg is V
+    assert cache.state is None
+    # the counter counts the prompt and every decode token (cache.py:251-260)
+    assert int(cache.global_token_counter) == S + 2 * om + 3
+
+
+def test_full_cache_with_q_cache_rejected(knobs):
+    """R_RATIO == 100 with a Q-cache (Q_RATIO > 0): the reference evicts at the
+    prefill and then stops compacting (cache.py:391-397, the physical cache
+    grows by torch.cat without bound).  The fixed slot layout cannot hold an
+    unbounded cache, so this combination is refused with a clear error."""
+    from qevict_b200 import QevictError
+    from qevict_b200.kv_cache import STICKYKVCache_LayerWise
+    import torch
+    knobs(OMEGA=16, SINK_TOKENS=16, LOCAL_NUM_TOKENS=32, Q_RATIO=10, QUANTIZATION_BIT_WIDTH=8,
+          GENERATION_CONFIG={"max_new_tokens": 40})
+    cfg = SimpleNamespace(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=1024)
+    cache = STICKYKVCache_LayerWise(50, 100, 0, 2, 1, cfg)
+    K = torch.zeros(1, 2, 16 + 16 * 6, 64)
+    with pytest.raises(QevictError, match="R_RATIO"):
+        cache((K, K), torch.zeros(1, 2, 1, K.shape[2]))

@@ -3,7 +3,18 @@
 Integer / index state (window ids, Q-cache codes, scales, zero points, the
 physical cache after every compaction) must match bit-for-bit whenever both
 sides consume the same score ledger; attention outputs and ledger values match
-within the stated tolerances.
+within the stated tolerances below.
+
+Two comparisons of the attention output are made at every step:
+
+* end to end: the kernel's output against the oracle run on its own logits;
+  the plain maximum absolute error is reported, and asserted on the
+  workloads' own input distributions (E2E_MAX_ABS);
+* given the same logits: the oracle is fed the kernel's rounded logits, and
+  every element must lie within a bound derived from the rounding points
+  (see ``output_bound``).  This is the check that holds on any input,
+  including the planted-spike stress runs, where a logit of ~7 makes one ulp
+  of the bf16 dot product (0.5 at |q.k| ~ 80) move a probability by 4 %.
 """
 
 import numpy as np
@@ -11,24 +22,47 @@ import pytest
 import torch
 
 from oracle import codec as ocodec
-from oracle.attention import decode_attention
+from oracle.attention import decode_attention, exact_dequant_qcache
 from oracle.numerics import rnd
 from oracle.sticky_state import OracleStickyLayer
 
 pytestmark = pytest.mark.gpu
 
 TD = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
-# Attention-output tolerance per KV dtype, given the same logits:
-#   |gpu - ref| <= atol + rtol * |ref| + ulp(out_main) + ulp(out_q).
-# The reference rounds the softmax probabilities to the KV dtype before P.V
-# (src/models/attention/ops.py:132), which the kernel does not (rtol: about two
-# ulps of the dtype), and rounds out_main and out_q separately before adding
-# them (ops.py:150), so either may land one ulp apart (the two ulp terms).
-TOL_OUT = {"fp32": (1e-5, 1e-5), "bf16": (2e-3, 1e-2), "fp16": (1e-3, 2e-3)}
+# Plain max-abs error of the attention output, kernel vs the oracle on its own
+# logits, asserted on the workloads' input distributions (fp32 and bf16 are
+# the target's stated figures; fp16 is 2^-3 of bf16's, as its ulp).
+E2E_MAX_ABS = {"fp32": 1e-5, "bf16": 2e-3, "fp16": 2.5e-4}
+# Unit roundoff of each dtype: the reference rounds every softmax probability
+# to the KV dtype before P.V (src/models/attention/ops.py:132).
+UNIT = {"fp32": 2.0 ** -24, "bf16": 2.0 ** -8, "fp16": 2.0 ** -11}
 # Vote-ledger tolerance (rtol, atol), given the same logits: the kernel and the
 # oracle round the same probabilities; only the fp32 normaliser's summation
 # order differs, which can flip a rounding tie by one ulp of the KV dtype.
 TOL_LEDGER = {"fp32": (1e-5, 1e-7), "bf16": (8e-3, 1e-6), "fp16": (2e-3, 1e-7)}
+
+
+def output_bound(ex, dt, fast_path):
+    """Per-element bound on |kernel - oracle| of the attention output, given the
+    same rounded logits (ex: the oracle's extras).  Terms, each derived from a
+    rounding point (A = sum_t p_t |v_t|, from the oracle):
+
+      * u_dt * A: the reference rounds each probability to the KV dtype before
+        P.V; the kernels multiply unrounded probabilities (bf16: a hi + lo
+        pair; fp32: exact);
+      * 2^-11 * A on the tensor-core path: it rounds p (and, in the Q-cache,
+        p * v_scale) to fp16 (bf16 for the hi part) once before the MMA;
+      * 2^-24 * sum_t p_t |v_t| (2 + 1.173 |x_t|): the fast exponential;
+      * 512 * 2^-24 * A: fp32 accumulation chains over tokens and the merge of
+        per-warp and per-CTA partial states;
+      * out_ulps: one ulp each at the reference's three roundings of out_main,
+        out_q and their sum (ops.py:150).
+    """
+    a = ex["abs_main"] + ex["abs_q"]
+    b = UNIT[dt] * a + 2.0 ** -24 * ex["abs_exp"] + 512 * 2.0 ** -24 * a
+    if fast_path:
+        b = b + 2.0 ** -11 * a
+    return 1.01 * b + ex["out_ulps"] + 1e-30
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -67,169 +101,324 @@ def test_codec_kernels_bit_exact(dt, bits, D):
     np.testing.assert_array_equal(vd.float().cpu().numpy(), ocodec.dequantize_from_quant(ovq, ovs, ovz, dt, bits))
 
 
-def _check_state(st, oracles, Kref, Vref, where):
+def _check_state(st, b, o, Kref, Vref, where, scores=True):
     ck, qc = st.counts()
-    for b, o in enumerate(oracles):
-        ids, sc = st.view_sticky(b)
-        oids, osc = o.sticky_ids()
-        assert ck[b] == oids.shape[1], where
-        np.testing.assert_array_equal(ids.numpy(), oids, err_msg=f"{where} b={b} sticky ids")
+    ids, sc = st.view_sticky(b)
+    oids, osc = o.sticky_ids()
+    assert ck[b] == oids.shape[1], where
+    np.testing.assert_array_equal(ids.numpy(), oids, err_msg=f"{where} b={b} sticky ids")
+    if scores:
         np.testing.assert_array_equal(sc.numpy(), osc, err_msg=f"{where} b={b} sticky scores")
-        q = st.view_q(b)
-        if o.q is None:
-            assert q is None, where
-        else:
-            assert qc[b] == o.q["ids"].shape[1], where
-            for key in ("ids", "scores", "kq", "vq", "ks", "kz", "vs", "vz"):
-                np.testing.assert_array_equal(q[key].numpy(), o.q[key], err_msg=f"{where} b={b} q.{key}")
-        K, V = st.view_kv(b)
-        np.testing.assert_array_equal(K.numpy(), Kref[b], err_msg=f"{where} b={b} K")
-        np.testing.assert_array_equal(V.numpy(), Vref[b], err_msg=f"{where} b={b} V")
-        np.testing.assert_array_equal(st.local_hist[b].cpu().numpy(), o.local_history, err_msg=f"{where} b={b} local_history")
-        arch = st.arch_valid[b].cpu().numpy()
-        got = sorted((int(w), int(h)) for h, w in zip(*np.nonzero(arch)))
-        assert got == sorted(o.meta.keys()), f"{where} b={b} archive"
+    q = st.view_q(b)
+    if o.q is None:
+        assert q is None, where
+    else:
+        assert qc[b] == o.q["ids"].shape[1], where
+        keys = ("ids", "scores", "kq", "vq", "ks", "kz", "vs", "vz") if scores else ("ids", "kq", "vq", "ks", "kz",
+                                                                                    "vs", "vz")
+        for key in keys:
+            np.testing.assert_array_equal(q[key].numpy(), o.q[key], err_msg=f"{where} b={b} q.{key}")
+    K, V = st.view_kv(b)
+    np.testing.assert_array_equal(K.numpy(), Kref, err_msg=f"{where} b={b} K")
+    np.testing.assert_array_equal(V.numpy(), Vref, err_msg=f"{where} b={b} V")
+    if scores:
+        np.testing.assert_array_equal(st.local_hist[b].cpu().numpy(), o.local_history,
+                                      err_msg=f"{where} b={b} local_history")
+    arch = st.arch_valid[b].cpu().numpy()
+    got = sorted((int(w), int(h)) for h, w in zip(*np.nonzero(arch)))
+    assert got == sorted(o.meta.keys()), f"{where} b={b} archive"
+
+
+def _window_sets(st, b, o):
+    """(gpu, oracle) window-id sets after a cycle: sticky ids and Q ids per head."""
+    ids, _ = st.view_sticky(b)
+    q = st.view_q(b)
+    g = (ids.numpy().tolist(), None if q is None else q["ids"].numpy().tolist())
+    oids, _ = o.sticky_ids()
+    r = (oids.tolist(), None if o.q is None else o.q["ids"].tolist())
+    return g, r
+
+
+def _same_sets(g, r):
+    """Same sticky ids per head and the same Q-cache window set per head (any order)."""
+    if g[0] != r[0]:
+        return False
+    if (g[1] is None) != (r[1] is None):
+        return False
+    return g[1] is None or all(sorted(a) == sorted(b) for a, b in zip(g[1], r[1]))
 
 
 def run_parity(dt, bits=8, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3, qw=4,
                n_prompt_windows=10, steps=256, seed=0, churn=True, maxW=64, reference_rounding=False,
-               max_context=4096):
+               max_context=4096, q_std=0.3, kv_std=1.0, check_b=None, same_ledger=True, e2e_max_abs=None):
     """Prefill + decode + eviction cycles on the GPU and in the oracle, step by step.
+
+    Inputs are seeded torch draws on the device (K, V ~ N(0, kv_std^2), queries
+    ~ N(0, q_std^2)); with churn=True, twice per window each query group is
+    aimed at a random cached key (main zone or Q-cache) so the ledger forces
+    promotions and demotions; with churn="scripted", each window picks one
+    Q-cache window per head and aims the first half of its queries at its keys
+    (promoting it, and pushing earlier promotions back out: every rebuild
+    path of the Q-cache is taken).  Sequences in check_b (default: all) are
+    replayed by the oracle.
 
     The tensor-core decode path dequantises the Q-cache exactly (code*scale + zp
     in fp32); the oracle then runs with dequant="exact".  The CUDA-core path
     (reference_rounding=True, and every shape the tensor-core kernel does not
     take) reproduces the reference's rounding; the oracle runs with
     dequant="reference".
+
+    same_ledger=True copies the kernel's vote ledger into the oracle before each
+    cycle, so window decisions must then match bit for bit; same_ledger=False
+    lets both run free and counts the cycles whose window sets agree (once a
+    sequence's sets differ, its caches differ and its later outputs are no
+    longer compared).
     """
     from qevict_b200 import StickyLayerState
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
     rng = np.random.default_rng(seed)
+    check_b = list(range(B)) if check_b is None else list(check_b)
     prompt = sink + n_prompt_windows * om
     st = StickyLayerState(B, H, G, D, om, sink, local, kw, qw, maxW, bits, TD[dt],
                           reference_rounding=reference_rounding)
-    dq_mode = "exact" if st.decode_path == 1 else "reference"
-    Kp = rnd(rng.standard_normal((B, H, prompt, D)), dt)
-    Vp = rnd(rng.standard_normal((B, H, prompt, D)), dt)
-    colsum = (rng.random((B, H, prompt)) * 4.0).astype(np.float32)
-    st.prefill(to_dev(Kp, dt), to_dev(Vp, dt), torch.tensor(colsum).cuda())
-    oracles, Kref, Vref = [], [], []
-    for b in range(B):
+    fast = st.decode_path == 1
+    dq_mode = "exact" if fast else "reference"
+
+    def draw(*shape, std=1.0):
+        return (torch.randn(*shape, generator=gen, device="cuda") * std).to(TD[dt])
+
+    Kp = draw(B, H, prompt, D, std=kv_std)
+    Vp = draw(B, H, prompt, D, std=kv_std)
+    colsum = torch.rand(B, H, prompt, generator=gen, device="cuda") * 4.0
+    st.prefill(Kp, Vp, colsum)
+    oracles, Kref, Vref = {}, {}, {}
+    for b in check_b:
         o = OracleStickyLayer(H, D, om, sink, local, kw, qw, dt, bits, max_windows=maxW,
                               max_context=max_context, window_sum="tree")
-        K, V = o.prefill(Kp[b], Vp[b], colsum[b][:, None, :], "fp32")
-        oracles.append(o)
-        Kref.append(K)
-        Vref.append(V)
-    _check_state(st, oracles, Kref, Vref, "prefill")
-    n_cycles = 0
+        K, V = o.prefill(Kp[b].float().cpu().numpy(), Vp[b].float().cpu().numpy(),
+                         colsum[b].cpu().numpy()[:, None, :], "fp32")
+        oracles[b], Kref[b], Vref[b] = o, K, V
+        _check_state(st, b, o, K, V, "prefill")
+    del Kp, Vp
+    stats = dict(cycles=0, e2e_max_abs=0.0, given_max_abs=0.0, bound_use=0.0, match=0, compared=0,
+                 diverged=set())
+    qdq = {}
+
+    def qcache_of(b):
+        o = oracles[b]
+        if o.q is None:
+            return None
+        qc = {k2: o.q[k2] for k2 in ("kq", "ks", "kz", "vq", "vs", "vz")}
+        if dq_mode == "exact":
+            key = id(o.q)
+            if qdq.get(b, (None,))[0] != key:
+                qdq[b] = (key, exact_dequant_qcache(o.q, bits))
+            qc["kdq"], qc["vdq"] = qdq[b][1]
+        return qc
+
     for step in range(steps):
-        q = rnd(rng.standard_normal((B, H * G, D)) * 0.3, dt)
-        if churn and step % om in (10, 40):
+        q = draw(B, H * G, D, std=q_std)
+        if churn == "scripted":
+            if step % om == 0:
+                target = {b: [int(rng.integers(1 << 30)) for _ in range(H)] for b in check_b}
+            for b in check_b:
+                o = oracles[b]
+                if step % om < om // 2 and o.q is not None:
+                    qd = ocodec.dequantize_from_quant(o.q["kq"], o.q["ks"], o.q["kz"], dt, bits)
+                    for h in range(H):
+                        key = qd[h, target[b][h] % qd.shape[1], rng.integers(om)]
+                        q[b, h * G:(h + 1) * G] = torch.tensor(key * 0.9, dtype=torch.float32,
+                                                               device="cuda").to(TD[dt])
+        elif churn and step % om in (10, 40):
             # plant attention spikes on a random cached token (main zone or Q-cache)
-            for b in range(B):
+            for b in check_b:
+                o = oracles[b]
                 for h in range(H):
-                    o = oracles[b]
                     if o.q is not None and rng.random() < 0.5:
                         qd = ocodec.dequantize_from_quant(o.q["kq"], o.q["ks"], o.q["kz"], dt, bits)
-                        j = rng.integers(qd.shape[1])
-                        t = rng.integers(om)
-                        key = qd[h, j, t]
+                        key = qd[h, rng.integers(qd.shape[1]), rng.integers(om)]
                     else:
                         key = Kref[b][h, rng.integers(Kref[b].shape[1])]
-                    q[b, h * G:(h + 1) * G] = rnd(key * rng.uniform(0.4, 0.9), dt)
-        kn = rnd(rng.standard_normal((B, H, D)), dt)
-        vn = rnd(rng.standard_normal((B, H, D)), dt)
-        qr = st.append(to_dev(q, dt), to_dev(kn, dt), to_dev(vn, dt))
+                    q[b, h * G:(h + 1) * G] = torch.tensor(key * rng.uniform(0.4, 0.9), dtype=torch.float32,
+                                                           device="cuda").to(TD[dt])
+        kn = draw(B, H, D, std=kv_std)
+        vn = draw(B, H, D, std=kv_std)
+        qr = st.append(q, kn, vn)
         out = torch.empty(B, H * G, D, dtype=TD[dt], device="cuda")
         st.attend(qr, out)
-        out_h = out.float().cpu().numpy()
-        due = False
-        for b in range(B):
+        due_all = []
+        for b in check_b:
             o = oracles[b]
-            Kc = np.concatenate([Kref[b], kn[b][:, None]], axis=1)
-            Vc = np.concatenate([Vref[b], vn[b][:, None]], axis=1)
-            qc = None
-            if o.q is not None:
-                qc = {k2: o.q[k2] for k2 in ("kq", "ks", "kz", "vq", "vs", "vz")}
-            oo, sc, qsc, ex = decode_attention(q[b], Kc, Vc, dt, qc, bits, dequant=dq_mode, return_extras=True)
-            # (1) the kernel's rounded logits equal the oracle's up to the accumulation-
-            #     order bound: one ulp of the KV dtype at the raw dot product (/ sqrt D)
-            #     plus one at the logit (plus the fp16 scale folding for Q tokens)
-            gl = st.view_logits(b).numpy()
-            assert gl.shape == ex["logits"].shape, (gl.shape, ex["logits"].shape)
-            dl = np.abs(gl.astype(np.float64) - ex["logits"])
-            bad = dl > ex["bound"]
-            assert not bad.any(), f"step {step} b={b}: {int(bad.sum())} logits beyond bound, worst {float((dl - ex['bound']).max())}"
-            # (2) everything downstream of the logits, driven by the kernel's logits
-            oo, sc, qsc, ex2 = decode_attention(q[b], Kc, Vc, dt, qc, bits, dequant=dq_mode,
-                                                logits_override=gl, return_extras=True)
-            tol = TOL_OUT[dt][0] + TOL_OUT[dt][1] * np.abs(oo) + ex2["out_ulps"]
-            err = np.abs(out_h[b] - oo)
-            assert (err <= tol).all(), (f"step {step} b={b} out: {int((err > tol).sum())} beyond tolerance, "
-                                        f"worst excess {float((err - tol).max())}")
+            qb = q[b].float().cpu().numpy()
+            Kc = np.concatenate([Kref[b], kn[b].float().cpu().numpy()[:, None]], axis=1)
+            Vc = np.concatenate([Vref[b], vn[b].float().cpu().numpy()[:, None]], axis=1)
+            qc = qcache_of(b)
+            oo, sc, qsc, ex = decode_attention(qb, Kc, Vc, dt, qc, bits, dequant=dq_mode, return_extras=True)
+            live = b not in stats["diverged"]
+            if live:
+                out_h = out[b].float().cpu().numpy()
+                # (1) end to end: the oracle on its own logits
+                stats["e2e_max_abs"] = max(stats["e2e_max_abs"], float(np.abs(out_h - oo).max()))
+                # (2) the kernel's rounded logits equal the oracle's up to the accumulation-
+                #     order bound: one ulp of the KV dtype at the raw dot product (/ sqrt D)
+                #     plus one at the logit (plus the fp16 scale folding for Q tokens)
+                gl = st.view_logits(b).numpy()
+                assert gl.shape == ex["logits"].shape, (gl.shape, ex["logits"].shape)
+                dl = np.abs(gl.astype(np.float64) - ex["logits"])
+                bad = dl > ex["bound"]
+                assert not bad.any(), (f"step {step} b={b}: {int(bad.sum())} logits beyond bound, "
+                                       f"worst {float((dl - ex['bound']).max())}")
+                # (3) everything downstream of the logits, driven by the kernel's logits
+                og, _, _, exg = decode_attention(qb, Kc, Vc, dt, qc, bits, dequant=dq_mode, logits_override=gl,
+                                                 return_extras=True)
+                err = np.abs(out_h - og)
+                tol = output_bound(exg, dt, fast)
+                stats["given_max_abs"] = max(stats["given_max_abs"], float(err.max()))
+                stats["bound_use"] = max(stats["bound_use"], float((err / tol).max()))
+                assert (err <= tol).all(), (f"step {step} b={b} out: {int((err > tol).sum())} beyond the bound, "
+                                            f"worst excess {float((err - tol).max())}")
             due = o.tally(Kc, sc, qsc, dt)
-            S = Kc.shape[1]
-            rt, at = TOL_LEDGER[dt]
-            gv = st.view_votes(b).numpy()
-            np.testing.assert_allclose(gv, o.votes[:, :S], rtol=rt, atol=at, err_msg=f"step {step} b={b} votes")
-            gq = st.view_q(b)
-            if o.q is not None:
-                np.testing.assert_allclose(gq["scores"].numpy(), o.q["scores"], rtol=rt, atol=at,
-                                           err_msg=f"step {step} b={b} q scores")
-            if due:
-                # same ledger on both sides before the cycle
-                o.votes[:, :S] = gv
+            if live:
+                S = Kc.shape[1]
+                rt, at = TOL_LEDGER[dt]
+                gv = st.view_votes(b).numpy()
+                np.testing.assert_allclose(gv, o.votes[:, :S], rtol=rt, atol=at, err_msg=f"step {step} b={b} votes")
+                gq = st.view_q(b)
                 if o.q is not None:
-                    o.q["scores"] = gq["scores"].numpy().copy()
+                    np.testing.assert_allclose(gq["scores"].numpy(), o.q["scores"], rtol=rt, atol=at,
+                                               err_msg=f"step {step} b={b} q scores")
+                if due and same_ledger:
+                    # same ledger on both sides before the cycle
+                    o.votes[:, :S] = gv
+                    if o.q is not None:
+                        o.q["scores"] = gq["scores"].numpy().copy()
             Kref[b], Vref[b] = Kc, Vc
-        assert due == st.cycle_due()
-        if due:
+            due_all.append(due)
+        assert all(d == st.cycle_due() for d in due_all)
+        if st.cycle_due():
             st.evict_cycle()
-            for b in range(B):
+            stats["cycles"] += 1
+            for b in check_b:
                 Kref[b], Vref[b] = oracles[b].cycle(Kref[b], Vref[b])
-            n_cycles += 1
-            _check_state(st, oracles, Kref, Vref, f"cycle {n_cycles}")
+                if same_ledger:
+                    _check_state(st, b, oracles[b], Kref[b], Vref[b], f"cycle {stats['cycles']}")
+                elif b not in stats["diverged"]:
+                    g, r = _window_sets(st, b, oracles[b])
+                    stats["compared"] += 1
+                    if _same_sets(g, r):
+                        stats["match"] += 1
+                    if g == r:
+                        _check_state(st, b, oracles[b], Kref[b], Vref[b], f"cycle {stats['cycles']}",
+                                     scores=False)
+                    else:
+                        # different windows, or the same Q windows in another
+                        # order: the caches are no longer comparable position
+                        # by position
+                        stats["diverged"].add(b)
     assert st.read_error() == 0
-    return n_cycles, oracles
+    print(f"\n[parity {dt} B={B} H={H} G={G} om={om} kw={kw} qw={qw} steps={steps} fast={fast}] "
+          f"e2e max-abs {stats['e2e_max_abs']:.3e}, given-logits max-abs {stats['given_max_abs']:.3e} "
+          f"(max err/bound {stats['bound_use']:.3f}), cycles {stats['cycles']}"
+          + ("" if same_ledger else f", free-running window sets equal in {stats['match']}/{stats['compared']}"))
+    if e2e_max_abs is not None:
+        assert stats["e2e_max_abs"] <= e2e_max_abs, f"e2e max-abs {stats['e2e_max_abs']} > {e2e_max_abs}"
+    stats["oracles"] = oracles
+    stats["fast"] = fast
+    # work items of the tensor-core kernel (32-token main tiles + Q windows)
+    # per CTA of its persistent grid (one CTA per SM); with >= 20 a CTA runs
+    # ten consumer warps instead of eight
+    items = B * H * (st.S_cap // 32 + qw)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    stats["items_per_cta"] = -(-items // min(sms, items))
+    return stats
 
 
 @pytest.mark.parametrize("dt", ["bf16", "fp32", "fp16"])
 def test_decode_and_cycles_vs_oracle(dt):
-    n, oracles = run_parity(dt)
-    assert n == 4
-    # the planted spikes must have exercised promotion (archive) and Q churn
-    assert any(len(o.meta) > 0 for o in oracles)
+    """Planted-spike stress run at a small shape: the given-logits bound holds at
+    every step and element; window decisions, Q-cache codes and the physical
+    cache are bit-exact after every cycle (fp32: plain max-abs <= 1e-5 too)."""
+    s = run_parity(dt, e2e_max_abs=E2E_MAX_ABS[dt] if dt == "fp32" else None)
+    assert s["cycles"] == 4
+    assert any(len(o.meta) > 0 for o in s["oracles"].values())
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+def test_rebuild_paths_all_taken(dt):
+    """Scripted churn: every Q-cache rebuild path of quantize_manager.py:148-327
+    runs on the GPU, each checked bit-exact against the oracle after its
+    cycle -- path A (a loser already in the Q-cache: raw copy), path B (fresh
+    quantisation of a demoted window, including the zero fill of a window
+    that is not at a block start of the old cache, :243-268) and path C
+    (re-quantisation of a window promoted earlier, with its archived scale
+    and zero point, :273-318)."""
+    s = run_parity(dt, B=2, H=4, kw=2, qw=4, steps=384, churn="scripted")
+    assert s["cycles"] == 6
+    pc = {k: sum(o.path_counts[k] for o in s["oracles"].values()) for k in ("A", "B", "B_zero", "C")}
+    print(f"rebuild paths taken: {pc}")
+    assert pc["A"] > 0 and pc["B"] > 0 and pc["B_zero"] > 0 and pc["C"] > 0, pc
 
 
 @pytest.mark.parametrize("dt", ["bf16", "fp16"])
 def test_decode_reference_rounding_mode(dt):
     """The CUDA-core kernel with the reference's Q-cache dequantisation rounding."""
-    n, oracles = run_parity(dt, reference_rounding=True)
-    assert n == 4
-    # the planted spikes must have exercised promotion (archive) and Q churn
-    assert any(len(o.meta) > 0 for o in oracles)
+    s = run_parity(dt, reference_rounding=True)
+    assert s["cycles"] == 4
+    assert any(len(o.meta) > 0 for o in s["oracles"].values())
 
 
 def test_decode_int4_qcache():
-    n, _ = run_parity("bf16", bits=4, steps=128)
-    assert n == 2
+    s = run_parity("bf16", bits=4, steps=128)
+    assert s["cycles"] == 2
 
 
-def test_decode_many_items_per_cta():
-    """The full-model layer shape at batch 4: 4 x 8 (sequence, head) pairs of 116
-    items (84 main-zone tiles of 32 tokens + 32 Q windows) = 3712 items over 148
-    CTAs, 26 per CTA -- enough that the tensor-core kernel runs with ten consumer
-    warps instead of eight.  Attention outputs, logits and ledger against the
-    oracle for a few steps (the cycle does not depend on the warp count)."""
-    n, _ = run_parity("bf16", B=4, H=8, local=512, kw=32, qw=32, n_prompt_windows=72, steps=6,
-                      churn=False, maxW=128, max_context=8192)
-    assert n == 0
+def test_decode_c1_shape_fp32():
+    """The single-layer fp32 workload's shape: 32 query / 8 KV heads, head_dim
+    128, omega 64, sink 64, local 256, 16 sticky + 16 Q windows, a 4096-token
+    prompt and 256 decode steps (4 cycles), q/K/V of the magnitude the
+    workload's projections give (N(0,1) hidden states through N(0, 0.02)
+    weights: std 0.02 * sqrt(4096) = 1.28), with planted spikes.  Plain
+    max-abs error of the output against the oracle on its own logits <= 1e-5."""
+    s = run_parity("fp32", B=1, H=8, G=4, D=128, sink=64, local=256, kw=16, qw=16, n_prompt_windows=63,
+                   steps=256, q_std=1.28, kv_std=1.28, maxW=128, max_context=8192, e2e_max_abs=E2E_MAX_ABS["fp32"])
+    assert s["cycles"] == 4
+
+
+def test_decode_c3_shape_bf16():
+    """The batch-64 microbenchmark's shape on the tensor-core path with ten
+    consumer warps per CTA: batch 64, 8 KV heads, group 4, 64 sink + 512 local
+    + 32 sticky windows (2048 tokens) + 64 INT8 Q windows (4096 tokens) per
+    sequence, K, V ~ N(0, 1), queries ~ N(0, 1); 130 steps (2 cycles).  Three
+    sequences (first, middle, last) are replayed by the oracle: plain max-abs
+    error <= 2e-3, the given-logits bound, and bit-exact state after both cycles."""
+    s = run_parity("bf16", B=64, H=8, G=4, D=128, sink=64, local=512, kw=32, qw=64, n_prompt_windows=104,
+                   steps=130, churn=False, q_std=1.0, kv_std=1.0, maxW=160, max_context=8192, check_b=(0, 31, 63),
+                   e2e_max_abs=E2E_MAX_ABS["bf16"])
+    assert s["cycles"] == 2 and s["fast"] and s["items_per_cta"] >= 20
+
+
+@pytest.mark.parametrize("dt", ["fp32", "bf16"])
+def test_free_running_window_sets(dt):
+    """No ledger copy: GPU and oracle each fold their own probabilities into
+    their own ledger and run their own cycles.  Reports the fraction of cycles
+    whose sticky and Q window sets agree (asserted >= 3/4)."""
+    s = run_parity(dt, B=4, H=4, G=4, sink=64, local=128, kw=4, qw=6, n_prompt_windows=16, steps=512,
+                   same_ledger=False, q_std=0.5)
+    assert s["cycles"] == 8
+    assert s["compared"] > 0 and s["match"] >= 0.75 * s["compared"], (s["match"], s["compared"])
 
 
 def test_decode_mha_and_small_budget():
     # G = 1 (MHA), sticky capacity larger than the prompt offers (growing phase)
-    n, _ = run_parity("fp16", G=1, kw=6, qw=2, n_prompt_windows=5, steps=192)
-    assert n == 3
+    s = run_parity("fp16", G=1, kw=6, qw=2, n_prompt_windows=5, steps=192)
+    assert s["cycles"] == 3
+
+
+def test_decode_smallest_omega():
+    """omega = 16, the smallest window the kernels take (CUDA-core decode path)."""
+    s = run_parity("bf16", D=64, om=16, sink=16, local=32, kw=3, qw=4, n_prompt_windows=12, steps=96)
+    assert s["cycles"] == 6
 
 
 def test_misaligned_prompt_rejected():
