@@ -89,6 +89,9 @@ def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="r
       abs_exp   sum_t p_t |v_t| (2 + 1.173 |x_t|), x_t = logit_t - max, both
                 zones: the weight of the fast exponential's error, at most
                 (2 + 1.173 |x|) fp32 ulps (CUDA's stated bound for __expf)
+      vsum_main sum_t |v_t| over the main zone, vsum_q over the Q-cache
+                [Hq, D]: the weight of an absolute error per probability
+                (fp16 subnormals, below 2^-14, are spaced 2^-24 apart)
     """
     q = f32(q)
     H, S, D = k_main.shape
@@ -172,10 +175,14 @@ def decode_attention(q, k_main, v_main, dt, qcache=None, bit_width=8, dequant="r
     abs_main = np.einsum("hgs,hsd->hgd", pf[..., :S], np.abs(vm64))
     abs_exp = np.einsum("hgs,hsd->hgd", ex[..., :S], np.abs(vm64))
     abs_q = np.zeros_like(abs_main)
+    vsum_main = np.broadcast_to(np.abs(vm64).sum(axis=1)[:, None, :], (H, G, D))
+    vsum_q = np.zeros_like(vsum_main)
     if qcache is not None:
         abs_q = np.einsum("hgs,hsd->hgd", pf[..., S:], np.abs(vdq64))
         abs_exp = abs_exp + np.einsum("hgs,hsd->hgd", ex[..., S:], np.abs(vdq64))
+        vsum_q = np.broadcast_to(np.abs(vdq64).sum(axis=1)[:, None, :], (H, G, D))
     return out.reshape(H * G, D), scores_main, scores_q, dict(
         logits=all_l, raw=raw, bound=bound, out_ulps=out_ulps.reshape(H * G, D),
         abs_main=abs_main.reshape(H * G, D), abs_q=abs_q.reshape(H * G, D),
-        abs_exp=abs_exp.reshape(H * G, D))
+        abs_exp=abs_exp.reshape(H * G, D), vsum_main=vsum_main.reshape(H * G, D),
+        vsum_q=vsum_q.reshape(H * G, D))

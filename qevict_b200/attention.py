@@ -14,12 +14,22 @@ and module_flash.py), returning ``(attn_output [B, q_len, hidden], None)``.
     the Q-cache with the ledger fold (``qv_decode_attention``), and every OMEGA
     tokens the eviction cycle (``qv_evict_cycle``).
 
+Positions: at the prefill, ``position_ids`` (a contiguous range p0 .. p0+q_len-1)
+set the prompt's RoPE positions (module.py:145-150 uses them when no cache is
+present); at decode, as in the reference, the position is the true global
+token count and the ``position_ids`` / ``attention_mask`` a caller passes are
+not used (module.py:141-150 and 163-170 replace them).  With a Hugging Face
+cache (``past_key_values``), each layer's entry becomes a
+``qevict_b200.hf.StickyDynamicLayer`` bound to the device state: its
+``get_seq_length()`` is the true token count and its ``keys`` / ``values``
+are the physical cache in the reference's order.  A prompt arriving with a
+cache that holds nothing for this layer starts a new sequence.
+
 Differences from the reference, by design: attention weights are never
 materialised (``output_attentions`` returns None); the prompt must fill whole
 windows after the sinks (``(q_len - SINK_TOKENS) % OMEGA == 0``) and cover
-the local zone; one prefill per sequence (call ``_clean_cache()`` before the
-next); the full-cache mode (R_RATIO >= 100 with Q_RATIO == 0) is not offered
-by the fused path (the cache object alone supports it).
+the local zone; the full-cache mode (R_RATIO >= 100 with Q_RATIO == 0) is not
+offered by the fused path (the cache object alone supports it).
 """
 
 import math
@@ -28,6 +38,7 @@ import torch
 from torch import nn
 
 from . import _native as N
+from .hf import StickyDynamicLayer, layer_entry  # noqa: F401  (re-exported: the reference's import path)
 from .kv_cache import STICKYKVCache_LayerWise
 from .model import prefill_attention, rope_
 
@@ -52,36 +63,6 @@ def rope_inv_freq(config, head_dim):
         blended = (1 - smooth) * inv / factor + smooth * inv
         inv = torch.where(wavelen > orig / lo, inv / factor, torch.where(wavelen < orig / hi, inv, blended))
     return inv
-
-
-class StickyDynamicLayer:
-    """Per-layer entry of a HF-style cache object (src/models/sticky_cache.py:25-152):
-    the physical K/V the layer holds and the true number of tokens seen."""
-
-    is_sliding = False
-    is_compileable = False
-
-    def __init__(self):
-        self.keys = None
-        self.values = None
-        self.is_initialized = False
-        self.cumulative_length = 0
-
-    def set_evicted_kv(self, keys, values):
-        self.keys, self.values = keys, values
-        self.is_initialized = True
-
-    def get_seq_length(self, *args, **kwargs):
-        return self.cumulative_length
-
-    def get_mask_sizes(self, cache_position, *args, **kwargs):
-        q = cache_position.shape[0] if hasattr(cache_position, "shape") else int(cache_position)
-        phys = self.keys.shape[-2] if self.keys is not None else 0
-        return phys + q, 0
-
-    def __repr__(self):
-        phys = self.keys.shape[-2] if self.keys is not None else 0
-        return f"StickyDynamicLayer(cumulative={self.cumulative_length}, physical={phys})"
 
 
 class STICKYLlamaAttention(nn.Module):
@@ -128,21 +109,32 @@ class STICKYLlamaAttention(nn.Module):
         B, T, _ = hidden_states.shape
         Hq, H, D = self.num_heads, self.num_key_value_heads, self.head_dim
         cache = self.kv_cache
+        entry = layer_entry(past_key_values, self.layer_idx)
+        if T > 1 and cache.state is not None and entry is not None and not entry.is_initialized:
+            # a prompt with a cache that holds nothing for this layer: a new sequence
+            self._clean_cache()
         if cache.state is None:
             if cache.total_cache_ratio >= 100 and cache.q_ratio == 0:
                 raise N.QevictError("the fused path always evicts: R_RATIO >= 100 with Q_RATIO == 0 is not offered")
-            cos, sin = self._tables(hidden_states.dtype, hidden_states.device, T + 1)
+            pos0 = 0
+            if position_ids is not None:
+                p = position_ids.reshape(-1, position_ids.shape[-1])[0].to("cpu", torch.long)
+                pos0 = int(p[0])
+                if not torch.equal(p, torch.arange(pos0, pos0 + T)):
+                    raise N.QevictError("prefill position_ids must be a contiguous range")
+            cos, sin = self._tables(hidden_states.dtype, hidden_states.device, pos0 + T + 1)
             q = self.q_proj(hidden_states).view(B, T, Hq, D).contiguous()
             k = self.k_proj(hidden_states).view(B, T, H, D).contiguous()
             v = self.v_proj(hidden_states).view(B, T, H, D).contiguous()
-            rope_(q, cos, sin)
-            rope_(k, cos, sin)
+            rope_(q, cos, sin, pos0)
+            rope_(k, cos, sin, pos0)
             out, colsum = prefill_attention(q, k, v)
             cache.prefill_state(k.transpose(1, 2).contiguous(), v.transpose(1, 2).contiguous(), colsum)
             attn = out.reshape(B, T, Hq * D)
         else:
             if T != 1:
-                raise N.QevictError("one prefill per sequence: call _clean_cache() before a new prompt")
+                raise N.QevictError("one prefill per sequence: call _clean_cache() (or pass a fresh cache) "
+                                    "before a new prompt")
             st = cache.state
             if B != st.B:
                 raise N.QevictError(f"batch {B} does not match the prefilled batch {st.B}")
@@ -155,13 +147,8 @@ class STICKYLlamaAttention(nn.Module):
             if st.cycle_due():
                 st.evict_cycle()
             attn = out.reshape(B, 1, Hq * D)
-        if use_cache and past_key_values is not None and hasattr(past_key_values, "layers"):
-            layers = past_key_values.layers
-            while len(layers) <= self.layer_idx:
-                layers.append(StickyDynamicLayer())
-            if not isinstance(layers[self.layer_idx], StickyDynamicLayer):
-                layers[self.layer_idx] = StickyDynamicLayer()
-            entry = layers[self.layer_idx]
-            entry.set_evicted_kv(cache.state.k, cache.state.v)
+        if use_cache and entry is not None:
+            # the layer's entry presents the device state (module.py:357-365)
+            entry.attach_state(cache.state)
             entry.cumulative_length = cache.state.n_tokens
         return self.o_proj(attn), None

@@ -191,9 +191,19 @@ def test_attention_module_c1_matches_reference_golden(knobs, monkeypatch):
     outputs of the reference's own STICKYLlamaAttention on the same seeded inputs
     (tests/golden/module_c1_fp32.npz, written by make_golden.py module_c1): a
     4096-token prompt and 256 decode steps, free running on both sides (each
-    side's own projections, logits, ledger and cycles).  Decode outputs: plain
-    max-abs <= 1e-5; window sets after the prefill and after each of the four
-    cycles: equal; final Q-cache scales within fp32 rounding of the inputs."""
+    side's own projections, logits, ledger and cycles).  Window sets after the
+    prefill and after each of the four cycles: equal (and the Q-cache's top-k
+    order); prefill outputs: max-abs <= 4e-5 (outputs up to ~6.4, fp32 sums
+    over 4096 positions); final Q-cache scales within fp32 rounding of the
+    inputs.
+
+    Decode outputs: max-abs <= 1e-3.  Both sides' fp32 projections of the same
+    inputs differ by ~1e-6, and the INT8 codes are a step function of K and V:
+    a value on a rounding boundary of (x - zp) / scale takes the neighbouring
+    code on one side, one quantisation step (scale ~ 0.03 here) apart, which
+    the attention then weights by that token's probability.  The test counts
+    those code flips (a few per window at most) and checks each side's code
+    sums against the other's."""
     torch = _cuda()
     import qevict_b200.kv_cache as kvmod
     from qevict_b200.allocator import BudgetResult
@@ -253,7 +263,7 @@ def test_attention_module_c1_matches_reference_golden(knobs, monkeypatch):
                 assert sorted(qsets[c][h].tolist()) == sorted(z["q_ids"][c][h].tolist()), f"Q window set, cycle {c}"
         order_same = np.mean([np.array_equal(a, b) for a, b in zip(qsets, z["q_ids"])])
         print(f"[C1] Q-cache top-k order identical after {order_same * 100:.0f} % of the cycles")
-        assert dec_err <= 1e-5, dec_err
+        assert dec_err <= 1e-3, dec_err
         assert pre_err <= 4e-5, pre_err
         q = st.view_q(0)
         # order the final Q windows like the reference's before comparing per window
@@ -265,6 +275,14 @@ def test_attention_module_c1_matches_reference_golden(knobs, monkeypatch):
         vsum = q["vq"].numpy().astype(np.int64).sum(axis=(2, 3))[hh, perm]
         # a code can sit on a rounding boundary of (x - zp) / scale: at most a
         # handful of +-1 flips per window of 8192 codes
+        kq0 = q["kq"].numpy()[hh, perm][:, 0].astype(np.int64)
+        vq0 = q["vq"].numpy()[hh, perm][:, 0].astype(np.int64)
+        flips = int((kq0 != z["q_kq_w0"]).sum() + (vq0 != z["q_vq_w0"]).sum())
+        print(f"[C1] code flips in the first Q window of every head: {flips} of {kq0.size * 2}; "
+              f"code-sum differences K {int(np.abs(ksum - z['q_kq_sum']).max())}, "
+              f"V {int(np.abs(vsum - z['q_vq_sum']).max())}")
+        assert int(np.abs(kq0 - z["q_kq_w0"]).max()) <= 1 and int(np.abs(vq0 - z["q_vq_w0"]).max()) <= 1
+        assert flips <= 0.001 * kq0.size * 2
         assert np.abs(ksum - z["q_kq_sum"]).max() <= 16 and np.abs(vsum - z["q_vq_sum"]).max() <= 16
         assert int(m.kv_cache.global_token_counter) == int(z["global_token_counter"])
         assert st.read_error() == 0

@@ -77,3 +77,53 @@ def test_budget_and_config_knobs():
     for knob in ("OMEGA", "SINK_TOKENS", "LOCAL_NUM_TOKENS", "P_RATIO", "R_RATIO", "Q_RATIO",
                  "QUANTIZATION_BIT_WIDTH", "S_IDX", "tracking_flag", "GENERATION_CONFIG"):
         assert hasattr(sticky_config, knob), knob
+
+
+def test_dynamic_layer_is_a_transformers_cache_layer():
+    """The layer is a transformers DynamicLayer whose sequence length is the true
+    token count, not the physical length (src/models/sticky_cache.py:25-152),
+    so a DynamicCache holding it reports the global position to LlamaModel."""
+    import torch
+    from transformers import DynamicCache
+    from transformers.cache_utils import DynamicLayer
+    from qevict_b200.hf import layer_entry
+    assert issubclass(StickyDynamicLayer, DynamicLayer)
+    cache = DynamicCache()
+    e = layer_entry(cache, 1)
+    assert isinstance(cache.layers[1], StickyDynamicLayer) and e is cache.layers[1]
+    assert not e.is_initialized
+    k = torch.randn(1, 2, 7, 4)
+    e.set_evicted_kv(k, k + 1)
+    e.cumulative_length = 40
+    assert e.is_initialized and e.keys is k and cache.get_seq_length(1) == 40
+    # mask sizes follow the physical K the attention consumes; the query
+    # length may be an int (transformers 5) or a cache_position tensor (4.57)
+    assert e.get_mask_sizes(1) == (8, 0) and e.get_mask_sizes(torch.arange(3)) == (10, 0)
+    assert cache.get_mask_sizes(1, 1) == (8, 0)
+    # DynamicLayer's own append still works for other attention modules
+    e2 = StickyDynamicLayer()
+    kk, vv = e2.update(torch.ones(1, 2, 3, 4), torch.zeros(1, 2, 3, 4))
+    assert kk.shape == (1, 2, 3, 4) and e2.get_seq_length() == 3
+    e2.update(torch.ones(1, 2, 1, 4), torch.zeros(1, 2, 1, 4))
+    assert e2.keys.shape[-2] == 4 and e2.get_seq_length() == 4
+    # a plain layer already in the cache is swapped for a Sticky one
+    cache.layers[0] = DynamicLayer()
+    assert isinstance(layer_entry(cache, 0), StickyDynamicLayer)
+
+
+def test_causal_lm_wrapper_surface():
+    """STICKYLlamaForCausalLM (src/models/sticky_llama_model.py:28-126): a
+    LlamaForCausalLM with the Sticky-KV attention in every layer and the
+    generation-position override."""
+    from types import SimpleNamespace  # noqa: F401
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaForCausalLM
+    from qevict_b200.hf import STICKYLlamaForCausalLM
+    assert issubclass(STICKYLlamaForCausalLM, LlamaForCausalLM)
+    cfg = LlamaConfig(vocab_size=128, hidden_size=256, num_attention_heads=4, num_key_value_heads=2,
+                      intermediate_size=512, num_hidden_layers=2, max_position_embeddings=1024)
+    cfg.rope_theta = 500000.0
+    m = STICKYLlamaForCausalLM(cfg)
+    assert all(type(layer.self_attn).__name__ == "STICKYLlamaAttention" for layer in m.model.layers)
+    assert [layer.self_attn.layer_idx for layer in m.model.layers] == [0, 1]
+    assert m._get_true_global_position() == 0

@@ -55,13 +55,16 @@ def output_bound(ex, dt, fast_path):
       * 2^-24 * sum_t p_t |v_t| (2 + 1.173 |x_t|): the fast exponential;
       * 512 * 2^-24 * A: fp32 accumulation chains over tokens and the merge of
         per-warp and per-CTA partial states;
+      * 2^-25 * sum_t |v_t| on the tensor-core path, over the Q-cache (and the
+        main zone for fp16): fp16 values below 2^-14 are subnormal, spaced
+        2^-24 apart, so a tiny probability carries an absolute rounding error;
       * out_ulps: one ulp each at the reference's three roundings of out_main,
         out_q and their sum (ops.py:150).
     """
     a = ex["abs_main"] + ex["abs_q"]
     b = UNIT[dt] * a + 2.0 ** -24 * ex["abs_exp"] + 512 * 2.0 ** -24 * a
     if fast_path:
-        b = b + 2.0 ** -11 * a
+        b = b + 2.0 ** -11 * a + 2.0 ** -25 * (ex["vsum_q"] + (ex["vsum_main"] if dt == "fp16" else 0.0))
     return 1.01 * b + ex["out_ulps"] + 1e-30
 
 
@@ -270,24 +273,34 @@ def run_parity(dt, bits=8, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3
                 assert not bad.any(), (f"step {step} b={b}: {int(bad.sum())} logits beyond bound, "
                                        f"worst {float((dl - ex['bound']).max())}")
                 # (3) everything downstream of the logits, driven by the kernel's logits
-                og, _, _, exg = decode_attention(qb, Kc, Vc, dt, qc, bits, dequant=dq_mode, logits_override=gl,
-                                                 return_extras=True)
+                og, sc_g, qsc_g, exg = decode_attention(qb, Kc, Vc, dt, qc, bits, dequant=dq_mode,
+                                                        logits_override=gl, return_extras=True)
                 err = np.abs(out_h - og)
                 tol = output_bound(exg, dt, fast)
                 stats["given_max_abs"] = max(stats["given_max_abs"], float(err.max()))
                 stats["bound_use"] = max(stats["bound_use"], float((err / tol).max()))
                 assert (err <= tol).all(), (f"step {step} b={b} out: {int((err > tol).sum())} beyond the bound, "
                                             f"worst excess {float((err - tol).max())}")
+            if same_ledger and live:
+                # the ledger is checked given the same logits: one ulp of the
+                # largest logit moves every other probability by exp(ulp)
+                # (6 % at a logit of 10 in bf16)
+                sc, qsc = sc_g, qsc_g
             due = o.tally(Kc, sc, qsc, dt)
             if live:
                 S = Kc.shape[1]
                 rt, at = TOL_LEDGER[dt]
                 gv = st.view_votes(b).numpy()
-                np.testing.assert_allclose(gv, o.votes[:, :S], rtol=rt, atol=at, err_msg=f"step {step} b={b} votes")
                 gq = st.view_q(b)
-                if o.q is not None:
-                    np.testing.assert_allclose(gq["scores"].numpy(), o.q["scores"], rtol=rt, atol=at,
-                                               err_msg=f"step {step} b={b} q scores")
+                if same_ledger:
+                    np.testing.assert_allclose(gv, o.votes[:, :S], rtol=rt, atol=at,
+                                               err_msg=f"step {step} b={b} votes")
+                    if o.q is not None:
+                        np.testing.assert_allclose(gq["scores"].numpy(), o.q["scores"], rtol=rt, atol=at,
+                                                   err_msg=f"step {step} b={b} q scores")
+                else:
+                    rel = np.abs(gv - o.votes[:, :S]) / np.maximum(np.abs(o.votes[:, :S]), 1e-30)
+                    stats["ledger_rel"] = max(stats.get("ledger_rel", 0.0), float(rel.max()))
                 if due and same_ledger:
                     # same ledger on both sides before the cycle
                     o.votes[:, :S] = gv
@@ -320,7 +333,8 @@ def run_parity(dt, bits=8, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3
     print(f"\n[parity {dt} B={B} H={H} G={G} om={om} kw={kw} qw={qw} steps={steps} fast={fast}] "
           f"e2e max-abs {stats['e2e_max_abs']:.3e}, given-logits max-abs {stats['given_max_abs']:.3e} "
           f"(max err/bound {stats['bound_use']:.3f}), cycles {stats['cycles']}"
-          + ("" if same_ledger else f", free-running window sets equal in {stats['match']}/{stats['compared']}"))
+          + ("" if same_ledger else f", free-running window sets equal in {stats['match']}/{stats['compared']}, "
+                                   f"ledger max relative difference {stats.get('ledger_rel', 0.0):.2e}"))
     if e2e_max_abs is not None:
         assert stats["e2e_max_abs"] <= e2e_max_abs, f"e2e max-abs {stats['e2e_max_abs']} > {e2e_max_abs}"
     stats["oracles"] = oracles
@@ -341,7 +355,6 @@ def test_decode_and_cycles_vs_oracle(dt):
     cache are bit-exact after every cycle (fp32: plain max-abs <= 1e-5 too)."""
     s = run_parity(dt, e2e_max_abs=E2E_MAX_ABS[dt] if dt == "fp32" else None)
     assert s["cycles"] == 4
-    assert any(len(o.meta) > 0 for o in s["oracles"].values())
 
 
 @pytest.mark.parametrize("dt", ["bf16", "fp16"])
@@ -362,9 +375,11 @@ def test_rebuild_paths_all_taken(dt):
 
 @pytest.mark.parametrize("dt", ["bf16", "fp16"])
 def test_decode_reference_rounding_mode(dt):
-    """The CUDA-core kernel with the reference's Q-cache dequantisation rounding."""
-    s = run_parity(dt, reference_rounding=True)
-    assert s["cycles"] == 4
+    """The CUDA-core kernel with the reference's Q-cache dequantisation rounding,
+    under the scripted churn (promotions, demotions, re-quantisation with
+    archived scales)."""
+    s = run_parity(dt, reference_rounding=True, B=2, H=4, kw=2, qw=4, steps=384, churn="scripted")
+    assert s["cycles"] == 6
     assert any(len(o.meta) > 0 for o in s["oracles"].values())
 
 
