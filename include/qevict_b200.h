@@ -149,7 +149,12 @@ int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t
  * (src/models/attention/ops.py:23-46, 74-169, 176-212), the vote tally
  * EvictionManager.tally_decode_scores (src/models/kv_cache/eviction_manager.py:198-203)
  * and QuantizationManager.accumulate_scores (src/models/kv_cache/quantize_manager.py:101-111).
- * q [B][G*H][D] rotated; out [B][G*H][D].  Advances step[0] by one token. */
+ * q [B][G*H][D] rotated; out [B][G*H][D].  Advances step[0] by one token.
+ * Launched as a programmatic dependent of the preceding kernel on the stream:
+ * it reads step[0], the slot tables and every cached token except the new one
+ * before that kernel has finished (only the new token and q are read after
+ * it), so the call must directly follow qv_rope_append on the same stream, or
+ * follow a kernel that writes none of this layer's state. */
 int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
                         void* workspace, size_t workspace_bytes, qv_stream_t stream);
 
@@ -163,8 +168,11 @@ int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void
  * QV_ESPACE with a message in qv_last_cuda_error().  The scratch is shared per
  * device, so calls that overlap in time race on it; the first call on a
  * device looks up the scratch address and should come before any capture or
- * timed loop.  Results are those of qv_decode_attention, except that the
- * logits are not exposed. */
+ * timed loop.  The address is cached per device and CUDA context: after a
+ * device reset the next call looks it up again (outside any capture).
+ * Ordering as qv_decode_attention (a programmatic dependent: directly after
+ * qv_rope_append on the same stream).  Results are those of
+ * qv_decode_attention, except that the logits are not exposed. */
 #define QV_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 int qv_decode_attention_noalloc(const qv_dims* d, const qv_layer* L, const void* q, void* out,
                                 qv_stream_t stream);

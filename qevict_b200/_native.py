@@ -13,6 +13,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "li
 QV_OK, QV_EINVAL, QV_ENOTALIGNED, QV_ESPACE, QV_ECUDA = 0, -1, -2, -3, -4
 QV_F32, QV_BF16, QV_F16 = 0, 1, 2
 QV_DERR_TABLE, QV_DERR_LAYOUT, QV_DERR_CAPACITY = 1, 2, 4
+QV_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024   # include/qevict_b200.h
 
 _ERRNAMES = {QV_EINVAL: "invalid argument", QV_ENOTALIGNED: "prompt/local zone not window-aligned",
              QV_ESPACE: "workspace too small", QV_ECUDA: "CUDA error"}

@@ -43,9 +43,21 @@ namespace qv {
 #ifndef QV_MM_CW_WIDE
 #define QV_MM_CW_WIDE 10
 #endif
-constexpr int MM_CW_NARROW = 8;
+#ifndef QV_MM_CW_NARROW
+#define QV_MM_CW_NARROW 8
+#endif
+constexpr int MM_CW_NARROW = QV_MM_CW_NARROW;
 constexpr int MM_CW_WIDE = QV_MM_CW_WIDE;
 static_assert(MM_CW_WIDE >= MM_CW_NARROW && MM_CW_WIDE <= 12, "consumer warps");
+// Consumer warps that share one item: each takes an equal run of its tokens
+// (main-zone tile: 2 m-tiles of 16 tokens; Q window: 4), so a stage is held
+// for a fraction of an item's compute time and more stages stay in flight.
+#ifndef QV_MM_SPLIT
+#define QV_MM_SPLIT 2
+#endif
+constexpr int MM_SPLIT = QV_MM_SPLIT;
+static_assert(MM_SPLIT == 1 || MM_SPLIT == 2, "warps per item");
+static_assert(MM_CW_NARROW % MM_SPLIT == 0 && MM_CW_WIDE % MM_SPLIT == 0, "whole warp groups");
 constexpr int MM_STAGE = 17408;                // bytes per stage (17 KB, 1024-aligned)
 constexpr int MM_MAXNS = 12;                   // max pipeline stages
 constexpr int MM_G = 8;                        // max GQA group
@@ -423,7 +435,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], MM_SPLIT);
         }
         fence_barrier_init();
         s_cnt[0] = s_cnt[1] = s_cnt[2] = s_cnt[3] = 0;
@@ -725,7 +737,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         if (skipped(i)) continue;
         const int kk_item = k++;
-        if (kk_item % CW != warp) continue;   // another warp's item
+        // items go round-robin to groups of MM_SPLIT warps; part = this warp's share
+        if (kk_item % (CW / MM_SPLIT) != warp / MM_SPLIT) continue;   // another group's item
+        const int part = warp % MM_SPLIT;
         const int s = kk_item % NS;
         // A warp that gives up waiting keeps walking the items (and joins every
         // named barrier) without computing, so no barrier is left unmatched.
@@ -741,32 +755,34 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         const uint32_t st = smem_u32(stages + s * MM_STAGE);
         const unsigned char* stp = stages + s * MM_STAGE;
         if (zone == 0) {
-            // ---------------- main zone: 32 tokens = 2 m-tiles -----------------
+            // ---------------- main zone: 32 tokens = 2 m-tiles, MMT per warp ----
             // two accumulators per m-tile (d < 64 and d >= 64) halve the chain
             // of dependent MMAs
-            float sc[2][4], sc2[2][4];
+            constexpr int MMT = 2 / MM_SPLIT;
+            const int mt0 = part * MMT;
+            float sc[MMT][4], sc2[MMT][4];
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int i = 0; i < MMT; ++i)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) sc[mt][r] = sc2[mt][r] = 0.f;
+                for (int r = 0; r < 4; ++r) sc[i][r] = sc2[i][r] = 0.f;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const int d = 16 * kk + 8 * (mi >> 1);
 #pragma unroll
-                for (int mt = 0; mt < 2; ++mt) {
-                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                for (int i = 0; i < MMT; ++i) {
+                    const int row = 16 * (mt0 + i) + (lane & 7) + 8 * (mi & 1);
                     uint32_t a[4], a2[4];
                     ldsm_x4(st + swz(row, d >> 3), a[0], a[1], a[2], a[3]);
                     ldsm_x4(st + 4096 + swz(row, d >> 3), a2[0], a2[1], a2[2], a2[3]);
-                    mma_kv<DT>(sc[mt], a, bq[kk]);
-                    mma_kv<DT>(sc2[mt], a2, bq[kk + 4]);
+                    mma_kv<DT>(sc[i], a, bq[kk]);
+                    mma_kv<DT>(sc2[i], a2, bq[kk + 4]);
                 }
             }
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
+            for (int i = 0; i < MMT; ++i)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) sc[mt][r] += sc2[mt][r];
-            float lg[2][4];   // per column: [mt*2 + rowhalf]
+                for (int r = 0; r < 4; ++r) sc[i][r] += sc2[i][r];
+            float lg[2][2 * MMT];   // per column: [i*2 + rowhalf]
             const int pos0 = MM_MT * j;
             // token t of this item is live iff off0 + t < lim: only the current
             // ring window has an unwritten tail
@@ -776,14 +792,14 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                 if (!mm_item_live(g, pos0 + 63 - off0, cw, 0)) lim = tv;
             }
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
-                const int tA = 16 * mt + gq, tB = tA + 8;
+            for (int i = 0; i < MMT; ++i) {
+                const int tA = 16 * (mt0 + i) + gq, tB = tA + 8;
                 const bool la = off0 + tA < lim, lb = off0 + tB < lim;
-                const float v0 = la ? logit_round<DT>(sc[mt][0]) : -INFINITY;
-                const float v1 = la ? logit_round<DT>(sc[mt][1]) : -INFINITY;
-                const float v2 = lb ? logit_round<DT>(sc[mt][2]) : -INFINITY;
-                const float v3 = lb ? logit_round<DT>(sc[mt][3]) : -INFINITY;
-                lg[0][2 * mt] = v0; lg[1][2 * mt] = v1; lg[0][2 * mt + 1] = v2; lg[1][2 * mt + 1] = v3;
+                const float v0 = la ? logit_round<DT>(sc[i][0]) : -INFINITY;
+                const float v1 = la ? logit_round<DT>(sc[i][1]) : -INFINITY;
+                const float v2 = lb ? logit_round<DT>(sc[i][2]) : -INFINITY;
+                const float v3 = lb ? logit_round<DT>(sc[i][3]) : -INFINITY;
+                lg[0][2 * i] = v0; lg[1][2 * i] = v1; lg[0][2 * i + 1] = v2; lg[1][2 * i + 1] = v3;
                 const int h0 = 2 * t4;
                 const size_t ia = ((size_t)bh * S_tot + pos0 + tA) * G + h0, ib = ((size_t)bh * S_tot + pos0 + tB) * G + h0;
                 if (h0 + 1 < G) {
@@ -794,26 +810,26 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     if (lb) lgp[ib] = Elt<DT>::t(v2);
                 }
             }
-            float p[2][4];
-            softmax_update(0, lg[0], p[0], 4);
-            softmax_update(1, lg[1], p[1], 4);
+            float p[2][2 * MMT];
+            softmax_update(0, lg[0], p[0], 2 * MMT);
+            softmax_update(1, lg[1], p[1], 2 * MMT);
             // P^T fragments per 16-token k-step (hi + lo halves for BF16)
 #pragma unroll
-            for (int mt = 0; mt < 2; ++mt) {
+            for (int i = 0; i < MMT; ++i) {
                 uint32_t bp[2], bl[2];
-                bp[0] = movm_t(pack2<DT>(p[0][2 * mt], p[1][2 * mt]));
-                bp[1] = movm_t(pack2<DT>(p[0][2 * mt + 1], p[1][2 * mt + 1]));
+                bp[0] = movm_t(pack2<DT>(p[0][2 * i], p[1][2 * i]));
+                bp[1] = movm_t(pack2<DT>(p[0][2 * i + 1], p[1][2 * i + 1]));
                 if (DT == QV_BF16) {
-                    const float r0 = p[0][2 * mt] - rnd<QV_BF16>(p[0][2 * mt]);
-                    const float r1 = p[1][2 * mt] - rnd<QV_BF16>(p[1][2 * mt]);
-                    const float r2 = p[0][2 * mt + 1] - rnd<QV_BF16>(p[0][2 * mt + 1]);
-                    const float r3 = p[1][2 * mt + 1] - rnd<QV_BF16>(p[1][2 * mt + 1]);
+                    const float r0 = p[0][2 * i] - rnd<QV_BF16>(p[0][2 * i]);
+                    const float r1 = p[1][2 * i] - rnd<QV_BF16>(p[1][2 * i]);
+                    const float r2 = p[0][2 * i + 1] - rnd<QV_BF16>(p[0][2 * i + 1]);
+                    const float r3 = p[1][2 * i + 1] - rnd<QV_BF16>(p[1][2 * i + 1]);
                     bl[0] = movm_t(pack2<DT>(r0, r1));
                     bl[1] = movm_t(pack2<DT>(r2, r3));
                 }
 #pragma unroll
                 for (int dt = 0; dt < 8; ++dt) {
-                    const int row = 16 * mt + (lane & 7) + 8 * (mi >> 1);
+                    const int row = 16 * (mt0 + i) + (lane & 7) + 8 * (mi >> 1);
                     const int d = 16 * dt + 8 * (mi & 1);
                     uint32_t a[4];
                     ldsm_x4_t(st + 8192 + (d >= 64 ? 4096 : 0) + swz(row, (d & 63) >> 3), a[0], a[1], a[2], a[3]);
@@ -860,37 +876,39 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             const float cr = zsum - 1024.f * ssum;
             const float corr0 = __shfl_sync(0xffffffffu, cr, 8 * t4);
             const float corr1 = __shfl_sync(0xffffffffu, cr, 8 * t4 + 4);
-            float sc[4][4];
+            constexpr int QMT = 4 / MM_SPLIT;   // m-tiles of this warp
+            const int qt0 = part * QMT;
+            float sc[QMT][4];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt)
+            for (int i = 0; i < QMT; ++i)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) sc[mt][r] = 0.f;
+                for (int r = 0; r < 4; ++r) sc[i][r] = 0.f;
 #pragma unroll
             for (int kk2 = 0; kk2 < 4; ++kk2) {
                 const int chunk = 2 * kk2 + (mi >> 1);
 #pragma unroll
-                for (int mt = 0; mt < 4; ++mt) {
-                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                for (int i = 0; i < QMT; ++i) {
+                    const int row = 16 * (qt0 + i) + (lane & 7) + 8 * (mi & 1);
                     uint32_t r[4];
                     ldsm_x4(st + swz(row, chunk), r[0], r[1], r[2], r[3]);
                     const uint32_t a0[4] = {__byte_perm(r[0], 0x64646464u, 0x5140), __byte_perm(r[1], 0x64646464u, 0x5140),
                                             __byte_perm(r[0], 0x64646464u, 0x5342), __byte_perm(r[1], 0x64646464u, 0x5342)};
                     const uint32_t a1[4] = {__byte_perm(r[2], 0x64646464u, 0x5140), __byte_perm(r[3], 0x64646464u, 0x5140),
                                             __byte_perm(r[2], 0x64646464u, 0x5342), __byte_perm(r[3], 0x64646464u, 0x5342)};
-                    mma_f16(sc[mt], a0, bk[2 * kk2]);
-                    mma_f16(sc[mt], a1, bk[2 * kk2 + 1]);
+                    mma_f16(sc[i], a0, bk[2 * kk2]);
+                    mma_f16(sc[i], a1, bk[2 * kk2 + 1]);
                 }
             }
             const int slot = j - P.n_main;
-            float lg[2][8];
+            float lg[2][2 * QMT];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int tA = 16 * mt + gq;
-                const float v0 = logit_round<DT>(sc[mt][0] + corr0);
-                const float v1 = logit_round<DT>(sc[mt][1] + corr1);
-                const float v2 = logit_round<DT>(sc[mt][2] + corr0);
-                const float v3 = logit_round<DT>(sc[mt][3] + corr1);
-                lg[0][2 * mt] = v0; lg[1][2 * mt] = v1; lg[0][2 * mt + 1] = v2; lg[1][2 * mt + 1] = v3;
+            for (int i = 0; i < QMT; ++i) {
+                const int tA = 16 * (qt0 + i) + gq;
+                const float v0 = logit_round<DT>(sc[i][0] + corr0);
+                const float v1 = logit_round<DT>(sc[i][1] + corr1);
+                const float v2 = logit_round<DT>(sc[i][2] + corr0);
+                const float v3 = logit_round<DT>(sc[i][3] + corr1);
+                lg[0][2 * i] = v0; lg[1][2 * i] = v1; lg[0][2 * i + 1] = v2; lg[1][2 * i + 1] = v3;
                 const int h0 = 2 * t4;
                 const size_t ia = ((size_t)bh * S_tot + g.S_cap + (size_t)slot * 64 + tA) * G + h0;
                 const size_t ib = ia + 8 * (size_t)G;
@@ -902,39 +920,39 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     lgp[ib] = Elt<DT>::t(v2);
                 }
             }
-            float p[2][8];
-            softmax_update(0, lg[0], p[0], 8);
-            softmax_update(1, lg[1], p[1], 8);
-            uint32_t bp[4][2];
+            float p[2][2 * QMT];
+            softmax_update(0, lg[0], p[0], 2 * QMT);
+            softmax_update(1, lg[1], p[1], 2 * QMT);
+            uint32_t bp[QMT][2];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int tA = 16 * mt + gq, tB = tA + 8;
+            for (int i = 0; i < QMT; ++i) {
+                const int tA = 16 * (qt0 + i) + gq, tB = tA + 8;
                 const float vsA = Elt<DT>::f(vs[tA]) * 1024.f, vsB = Elt<DT>::f(vs[tB]) * 1024.f;
                 const float vzA = Elt<DT>::f(vz[tA]), vzB = Elt<DT>::f(vz[tB]);
                 // P'' = p * v_scale * 1024 in f16; corrections use the rounded values
-                const float pa0 = f16r(p[0][2 * mt] * vsA), pa1 = f16r(p[1][2 * mt] * vsA);
-                const float pb0 = f16r(p[0][2 * mt + 1] * vsB), pb1 = f16r(p[1][2 * mt + 1] * vsB);
+                const float pa0 = f16r(p[0][2 * i] * vsA), pa1 = f16r(p[1][2 * i] * vsA);
+                const float pb0 = f16r(p[0][2 * i + 1] * vsB), pb1 = f16r(p[1][2 * i + 1] * vsB);
                 spp[0] += pa0 + pb0;
                 spp[1] += pa1 + pb1;
-                svz[0] += p[0][2 * mt] * vzA + p[0][2 * mt + 1] * vzB;
-                svz[1] += p[1][2 * mt] * vzA + p[1][2 * mt + 1] * vzB;
-                bp[mt][0] = movm_t(pack2<QV_F16>(pa0, pa1));
-                bp[mt][1] = movm_t(pack2<QV_F16>(pb0, pb1));
+                svz[0] += p[0][2 * i] * vzA + p[0][2 * i + 1] * vzB;
+                svz[1] += p[1][2 * i] * vzA + p[1][2 * i + 1] * vzB;
+                bp[i][0] = movm_t(pack2<QV_F16>(pa0, pa1));
+                bp[i][1] = movm_t(pack2<QV_F16>(pb0, pb1));
             }
 #pragma unroll
             for (int dt2 = 0; dt2 < 4; ++dt2) {
                 const int chunk = 2 * dt2 + (mi >> 1);
 #pragma unroll
-                for (int mt = 0; mt < 4; ++mt) {
-                    const int row = 16 * mt + (lane & 7) + 8 * (mi & 1);
+                for (int i = 0; i < QMT; ++i) {
+                    const int row = 16 * (qt0 + i) + (lane & 7) + 8 * (mi & 1);
                     uint32_t r[4];
                     ldsm_x4_t(st + 8192 + swz(row, chunk), r[0], r[1], r[2], r[3]);
                     const uint32_t a0[4] = {__byte_perm(r[0], 0x64646464u, 0x5240), __byte_perm(r[0], 0x64646464u, 0x5341),
                                             __byte_perm(r[1], 0x64646464u, 0x5240), __byte_perm(r[1], 0x64646464u, 0x5341)};
                     const uint32_t a1[4] = {__byte_perm(r[2], 0x64646464u, 0x5240), __byte_perm(r[2], 0x64646464u, 0x5341),
                                             __byte_perm(r[3], 0x64646464u, 0x5240), __byte_perm(r[3], 0x64646464u, 0x5341)};
-                    mma_f16(o[2 * dt2], a0, bp[mt]);
-                    mma_f16(o[2 * dt2 + 1], a1, bp[mt]);
+                    mma_f16(o[2 * dt2], a0, bp[i]);
+                    mma_f16(o[2 * dt2 + 1], a1, bp[i]);
                 }
             }
         }
@@ -1054,8 +1072,8 @@ size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
 
 int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s) {
     MmPlan P = mm_plan(g);
-    // a consumer warp may wait on a stage only one fill ahead of it: stages >= warps
-    if (P.pmax > 64 || P.ns < P.cw) return QV_EINVAL;
+    // a warp group may wait on a stage only one fill ahead of it: stages >= groups
+    if (P.pmax > 64 || P.ns < P.cw / MM_SPLIT) return QV_EINVAL;
     size_t op, ol;
     mm_ws_bytes(g, &op, &ol);
     char* base = reinterpret_cast<char*>(ws);

@@ -15,7 +15,16 @@
 // their streams) race on it and give wrong results.  The first call on each
 // device looks up the array's address (cudaGetSymbolAddress, which may
 // initialise the module on that device); make that first call before any
-// stream capture or latency-critical loop begins.
+// stream capture or latency-critical loop begins.  The address is cached per
+// device together with the CUDA context it was looked up in; a call made in
+// another context (after cudaDeviceReset, or once the primary context has
+// been torn down and created again) looks it up afresh.
+//
+// Like qv_decode_attention, the call is launched as a programmatic dependent:
+// it reads the slot tables and cached K/V before the preceding kernel on the
+// stream has finished, so it must directly follow qv_rope_append on the same
+// stream, or a kernel that writes none of the layer's state.
+#include <cudaTypedefs.h>
 #include <mutex>
 #include <stdio.h>
 
@@ -27,20 +36,41 @@ static __device__ __align__(256) unsigned char g_decode_scratch[QV_NOALLOC_SCRAT
 
 static constexpr int kMaxDevices = 64;
 static void* g_scratch_addr[kMaxDevices];
+static CUcontext g_scratch_ctx[kMaxDevices];
 static std::mutex g_scratch_mu;
 
-// Address of g_decode_scratch on the current device, looked up once per device.
+static PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+    static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    }
+    return fn;
+}
+
+// Address of g_decode_scratch on the current device, looked up once per
+// device and context.
 static int scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_cuda_error(e);
     if (dev < 0 || dev >= kMaxDevices) return QV_EINVAL;
+    auto get = ctx_get_current();
+    if (!get) return QV_ECUDA;
+    CUcontext ctx = nullptr;
+    if (get(&ctx) != CUDA_SUCCESS) return QV_ECUDA;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!ctx || !g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
+        // the lookup makes the device's primary context current if no context was
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_decode_scratch);
         if (e != cudaSuccess) return set_cuda_error(e);
+        if (get(&ctx) != CUDA_SUCCESS || !ctx) return QV_ECUDA;
         g_scratch_addr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_addr[dev];
     return QV_OK;

@@ -123,7 +123,7 @@ def test_hf_llama_decode_matches_oracle(sticky_model, monkeypatch):
         oracles.append(o)
         KV.append((Kr, Vr))
     tok = out.logits[:, -1].argmax(-1, keepdim=True)
-    e2e, bound_use, cycles = 0.0, 0.0, 0
+    e2e, e2e_ulp, bound_use, cycles = 0.0, 0.0, 0.0, 0
     steps = 2 * OM + 2
     for step in range(steps):
         pos = PROMPT + step
@@ -148,6 +148,11 @@ def test_hf_llama_decode_matches_oracle(sticky_model, monkeypatch):
             ref, _, _ = decode_attention(qn, Kc, Vc, "bf16", qc, dequant="exact")
             got = cap[f"o{li}"][0, 0].reshape(H * G, D)
             e2e = max(e2e, float(np.abs(got - ref).max()))
+            # plain max-abs beyond one bf16 ulp of the reference value: a pre-rounding
+            # difference of a hair can put the two results one ulp apart (3.9e-3 at
+            # |out| in [0.5, 1)); for outputs below 0.5 this is max-abs <= 2e-3 itself
+            ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - 7)
+            e2e_ulp = max(e2e_ulp, float((np.abs(got - ref) - ulp).max()))
             due = o.tokens_since + 1 == OM
             if not due:
                 # the kernel's logits are only readable before the cycle rewrites the layout
@@ -181,10 +186,10 @@ def test_hf_llama_decode_matches_oracle(sticky_model, monkeypatch):
                 rt, at = 8e-3, 1e-6
                 np.testing.assert_allclose(st.view_votes(0).numpy(), o.votes[:, :Kc.shape[1]], rtol=rt, atol=at)
             KV[li] = (Kc, Vc)
-    print(f"\n[HF Llama 2 layers bf16] decode max-abs vs oracle {e2e:.3e}, given-logits bound use "
-          f"{bound_use:.3f}, cycles (all layers) {cycles}")
+    print(f"\n[HF Llama 2 layers bf16] decode max-abs vs oracle {e2e:.3e} ({e2e_ulp:.3e} beyond one ulp of the "
+          f"reference), given-logits bound use {bound_use:.3f}, cycles (all layers) {cycles}")
     assert cycles == 2 * len(layers)
-    assert e2e <= 2e-3
+    assert e2e_ulp <= 2e-3
     for layer in layers:
         assert layer.self_attn.kv_cache.state.read_error() == 0
 

@@ -33,7 +33,7 @@ def _pair(dtype, B=2, H=2, G=4, D=128, om=64, sink=64, local=128, kw=3, qw=4, n_
     cs = torch.rand(B, H, S, generator=g, device="cuda") * 4
     states = []
     for _ in range(2):
-        st = StickyLayerState(B, H, G, D, om, sink, local, kw, qw, 64, 8, dtype)
+        st = StickyLayerState(B, H, G, D, om, sink, local, kw, qw, 128, 8, dtype)
         st.prefill(k, v, cs)
         states.append(st)
     return states, g
@@ -46,9 +46,16 @@ def _noalloc(st, q_rot, out):
     st.n_tokens += 1
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_noalloc_matches_workspace_entry_point(dtype):
-    (a, b), g = _pair(dtype)
+@pytest.mark.parametrize("dtype,shape", [
+    (torch.bfloat16, {}),
+    (torch.float32, {}),
+    # the largest shape the header names for the 8 MiB scratch: batch 8 at the
+    # Llama-3-8B layer shape, 32 sticky + 32 Q windows of 64, local 512
+    (torch.bfloat16, dict(B=8, H=8, G=4, local=512, kw=32, qw=32, n_windows=72)),
+])
+def test_noalloc_matches_workspace_entry_point(dtype, shape):
+    (a, b), g = _pair(dtype, **shape)
+    assert int(N.lib().qv_decode_workspace_bytes(ctypes.byref(a.dims))) <= N.QV_NOALLOC_SCRATCH_BYTES
     B, HG, D = a.B, a.H * a.G, a.D
     for step in range(2):
         q = torch.randn(B, HG, D, generator=g, device="cuda").to(dtype) * 0.3
