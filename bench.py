@@ -555,6 +555,114 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+TP_PROMPT = 131072
+TP_WORKLOAD = ("Llama-3-8B-shaped full-model decode with KV-head tensor parallelism over the job's GPUs (q/k/v and "
+               "gate/up column-parallel, o_proj and down row-parallel with one NCCL all-reduce each, vocab-parallel "
+               "LM head), bf16 random init, batch 1, 131072-token prompt (prefill lane: causal attention + per-key "
+               "column sums seeding the ledger), then decode; Sticky-KV omega 64, sink 64, local 512, sticky 4096, "
+               "INT8 Q-cache 8192")
+
+
+def run_tp(args):
+    """The long-context workload split by KV head over the job's ranks (strong scaling)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qevict_b200.model import LlamaShape, StickyShape
+    from qevict_b200.tp_model import TpStickyLlamaDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev,
+                            rank=rank, world_size=world) if world > 1 else None
+    torch.backends.cuda.matmul.allow_tf32 = False
+    prompt = args.tp_prompt
+    sticky = StickyShape(k_windows=64, q_windows=128)
+    model = TpStickyLlamaDecoder(LlamaShape(), sticky, rank, world, batch=1, max_pos=prompt + 4096, device=dev,
+                                 seed=1234)
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    ids = torch.randint(0, model.s.vocab, (1, prompt), generator=g, device=dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    model.prefill(ids)
+    torch.cuda.synchronize()
+    prefill_s = max_over_ranks_on(time.perf_counter() - t0, world, dev)
+    del ids
+    W, K = args.warmup, args.steps
+    om = sticky.omega
+    for _ in range(min(3, W)):
+        model.step_eager()
+    torch.cuda.synchronize()
+    model.capture()
+    plain_ms, cycle_ms = [], []
+    n_warm = min(3, W)
+    st0 = model.states[0]
+    while n_warm < W or not cycle_ms or (st0.n_tokens - st0.prompt_len) % om != 0:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        cyc = model.step_graph()
+        b.record()
+        b.synchronize()
+        (cycle_ms if cyc else plain_ms).append(a.elapsed_time(b))
+        n_warm += 1
+    plain_med = statistics.median(plain_ms[-32:]) if plain_ms else 0.0
+    cycle_extra_ms = max_over_ranks_on(max(0.0, statistics.median(cycle_ms) - plain_med), world, dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cycles = 0
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(max(1, int(math.ceil(1200.0 / max(1e-3, om * plain_med)))) * om):
+            model.step_graph()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(K):
+            cycles += model.step_graph()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    raw_ms = max_over_ranks_on(start.elapsed_time(end), world, dev)
+    added_ms = (K / om - cycles) * cycle_extra_ms
+    ms = raw_ms + added_ms
+    # per layer: gemv x4, rope_append, decode_mma, fold, add_rmsnorm x2, silu_mul (+ torch's
+    # argmax pieces per step); per cycle and layer: count + ext
+    launches = K * (10 * model.s.layers + 3) + cycles * 2 * model.s.layers
+    kv = model.s.layers * model.attention_bytes_per_layer((om + 1) / 2)
+    step_bytes = model.weight_bytes() + kv
+    peak, peak_kind = peaks()
+    if rank == 0:
+        line = {"metric": METRIC, "value": K / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: random-init weights N(0,0.02), uniform random prompt token ids",
+                "config": {"workload": TP_WORKLOAD, "prompt_tokens": prompt, "batch": 1,
+                           "parallelism": f"kv-head tensor parallel x{world} ({model.hl} KV head(s) per GPU)",
+                           "prefill_s": round(prefill_s, 2), "eviction_cycles_timed": cycles,
+                           "cycle_rate": {"cycles_at_true_rate": K / om, "cycle_step_extra_ms": cycle_extra_ms,
+                                          "added_ms": added_ms, "device_timed_ms": raw_ms},
+                           "collectives_per_step": {"all_reduce_sum_bf16_hidden": 2 * model.s.layers,
+                                                    "all_reduce_max_int64": 1,
+                                                    "all_reduce_min_int32_per_cycle": model.s.layers}},
+                "step_roofline": {"bound": "hbm", "bytes_per_step_per_gpu": step_bytes,
+                                  "achieved": step_bytes / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                                  "frac": step_bytes / (ms / K * 1e-3) / 1e9 / peak, "peak_source": peak_kind},
+                "gpu_launches": launches, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    model.graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -562,11 +670,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=8, help="tokens the host baseline times (rank 0, N=1)")
+    ap.add_argument("--tp", action="store_true", help="the long-context workload, KV heads split over the ranks")
+    ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_ours(args)
 
