@@ -40,13 +40,27 @@ class TorchDistExchange:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self._staging = {}
 
     def gather_heads(self, local, out):
-        """local [B, hl, D] of this rank -> out [B, world*hl, D], heads in rank order."""
+        """local [B, hl, D] of this rank -> out [B, world*hl, D], heads in rank order.
+
+        One all_gather_into_tensor into a staging buffer kept across calls
+        ([world * B, hl, D]: no allocation per token, so the call can be
+        captured in a CUDA graph), then one copy into out's head order (the
+        copy is a no-op reshape when B == 1)."""
         B, hl, D = local.shape
-        parts = [torch.empty_like(local) for _ in range(self.world)]
-        self.dist.all_gather(parts, local.contiguous(), group=self.group)
-        out.view(B, self.world, hl, D).copy_(torch.stack(parts, dim=1))
+        key = (B, hl, D, local.dtype, local.device)
+        buf = self._staging.get(key)
+        if buf is None:
+            # the concatenated form [world * B, hl, D] (every backend takes it)
+            buf = torch.empty(self.world * B, hl, D, dtype=local.dtype, device=local.device)
+            self._staging[key] = buf
+        self.dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
+        if B == 1:
+            out.view(self.world, hl, D).copy_(buf)
+        else:
+            out.view(B, self.world, hl, D).copy_(buf.view(self.world, B, hl, D).permute(1, 0, 2, 3))
 
     def min_(self, t):
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN, group=self.group)
