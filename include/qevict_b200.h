@@ -158,6 +158,22 @@ int qv_rope(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t
 int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
                         void* workspace, size_t workspace_bytes, qv_stream_t stream);
 
+/* qv_decode_attention in two launches, so that the vote-ledger fold can run
+ * off the critical path (on another stream, beside the next projections).
+ * No counterpart in the reference (its tally follows its attention in one
+ * Python call, eviction_manager.py:198-203).
+ * qv_decode_attention_nofold writes out and advances step[0]; the fold of this
+ * step's probabilities into votes / q_score is left pending.
+ * qv_decode_fold performs the pending fold.  It must be ordered after the
+ * nofold call (same stream, or an event) and before the next qv_rope_append,
+ * qv_decode_attention* or qv_evict_cycle on this layer, and before the
+ * workspace is used again.  On the CUDA-core path (qv_decode_path() == 0) the
+ * nofold call folds the ledger itself and qv_decode_fold does nothing. */
+int qv_decode_attention_nofold(const qv_dims* d, const qv_layer* L, const void* q, void* out,
+                               void* workspace, size_t workspace_bytes, qv_stream_t stream);
+int qv_decode_fold(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                   qv_stream_t stream);
+
 /* qv_decode_attention without a workspace argument; no counterpart in the
  * reference.  For callers that cannot allocate device memory between decode
  * steps (a foreign-language host holding only the layer's pointers, or a

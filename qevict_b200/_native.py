@@ -64,6 +64,8 @@ def lib():
         "qv_rope_append": (ctypes.c_int, [D, Lp, vp, vp, vp, vp, vp, vp, vp]),
         "qv_decode_attention": (ctypes.c_int, [D, Lp, vp, vp, vp, sz, vp]),
         "qv_decode_attention_noalloc": (ctypes.c_int, [D, Lp, vp, vp, vp]),
+        "qv_decode_attention_nofold": (ctypes.c_int, [D, Lp, vp, vp, vp, sz, vp]),
+        "qv_decode_fold": (ctypes.c_int, [D, Lp, vp, sz, vp]),
         "qv_rope": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, i32, vp]),
         "qv_evict_cycle": (ctypes.c_int, [D, Lp, vp, sz, vp]),
         "qv_evict_cycle_count": (ctypes.c_int, [D, Lp, vp, sz, vp, vp]),
@@ -99,7 +101,7 @@ def exported_symbols():
     return ["qv_ring_windows", "qv_main_capacity", "qv_decode_workspace_bytes", "qv_decode_path",
             "qv_decode_logits_offset",
             "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention",
-            "qv_decode_attention_noalloc", "qv_evict_cycle",
+            "qv_decode_attention_noalloc", "qv_decode_attention_nofold", "qv_decode_fold", "qv_evict_cycle",
             "qv_evict_cycle_count", "qv_evict_cycle_ext",
             "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_gemv",

@@ -339,7 +339,7 @@ __global__ void rope_tokens_kernel(int heads, int D, void* __restrict__ x, const
 // tensor-core kernel for the production shape (decode_mma.cu)
 bool mm_supported(const Geo& g);
 size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits);
-int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s);
+int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s, int mode);
 
 }  // namespace qv
 
@@ -417,11 +417,12 @@ static void launch_decode(const Geo& g, const qv_layer& L, const void* q, Decode
     else decode_split_kernel<DT, D, 4><<<grid, DEC_THREADS, 0, s>>>(g, L, q, ws, out);
 }
 
-extern "C" int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
-                                   void* workspace, size_t workspace_bytes, qv_stream_t stream) {
+// mode: 0 = attention + ledger fold, 1 = attention (fold pending), 2 = the pending fold
+static int decode_attention_mode(const qv_dims* d, const qv_layer* L, const void* q, void* out, void* workspace,
+                                 size_t workspace_bytes, qv_stream_t stream, int mode) {
     int rc = validate_dims(d);
     if (rc) return rc;
-    if (!L || !q || !out || !workspace) return QV_EINVAL;
+    if (!L || !workspace || (mode != 2 && (!q || !out))) return QV_EINVAL;
     Geo g = make_geo(d);
     size_t op, ol, tot;
     DecodeWs ws;
@@ -431,8 +432,10 @@ extern "C" int qv_decode_attention(const qv_dims* d, const qv_layer* L, const vo
     if (mm_supported(g)) {
         size_t a2, b2;
         if (workspace_bytes < mm_ws_bytes(g, &a2, &b2)) return QV_ESPACE;
-        return mm_launch(g, *L, q, out, workspace, s);
+        return mm_launch(g, *L, q, out, workspace, s, mode);
     }
+    // the CUDA-core kernel folds the ledger inside the attention launch
+    if (mode == 2) return QV_OK;
     char* base = reinterpret_cast<char*>(workspace);
     ws.tickets = reinterpret_cast<int*>(base);
     ws.partial = reinterpret_cast<float*>(base + op);
@@ -443,4 +446,19 @@ extern "C" int qv_decode_attention(const qv_dims* d, const qv_layer* L, const vo
         default: if (g.D == 128) launch_decode<QV_F16, 128>(g, *L, q, ws, out, s); else launch_decode<QV_F16, 64>(g, *L, q, ws, out, s); break;
     }
     return check_launch();
+}
+
+extern "C" int qv_decode_attention(const qv_dims* d, const qv_layer* L, const void* q, void* out,
+                                   void* workspace, size_t workspace_bytes, qv_stream_t stream) {
+    return decode_attention_mode(d, L, q, out, workspace, workspace_bytes, stream, 0);
+}
+
+extern "C" int qv_decode_attention_nofold(const qv_dims* d, const qv_layer* L, const void* q, void* out,
+                                          void* workspace, size_t workspace_bytes, qv_stream_t stream) {
+    return decode_attention_mode(d, L, q, out, workspace, workspace_bytes, stream, 1);
+}
+
+extern "C" int qv_decode_fold(const qv_dims* d, const qv_layer* L, void* workspace, size_t workspace_bytes,
+                              qv_stream_t stream) {
+    return decode_attention_mode(d, L, nullptr, nullptr, workspace, workspace_bytes, stream, 2);
 }

@@ -197,33 +197,37 @@ __device__ __forceinline__ float group_prob_sum4(uint2 u, const float* sM, const
 }
 
 // Shared scratch of one combine unit, in floats: per-head partial maxima and
-// weights [G][2*64], per-head totals, the two output accumulators [2][G*128]
-// and one liveness code per 64-token block of the unit.
+// weights [G][2*64], per-head totals and one liveness code per 64-token block
+// of the unit.
 constexpr int MM_CMB_MAXBLK = 1024;
-constexpr int MM_CMB_SMEM = 2 * MM_G * 128 + 2 * MM_G + 2 * MM_G * 128 + MM_CMB_MAXBLK / 4;
+constexpr int MM_CMB_SMEM = 2 * MM_G * 128 + 2 * MM_G + MM_CMB_MAXBLK / 4;
 
-// One combine unit: merge the per-CTA partials of one (sequence, KV head) bh,
-// write this unit's slice of its output, and fold the exact probabilities of
-// this unit's 64-token blocks into the vote ledger / Q-window scores.  Run by
-// nthr threads (tid < nthr, nthr a multiple of 32 and >= 32*G) that synchronise
-// with sync(); N0 is the token count the attention pass saw (new token
-// included).  Written for latency: a thread issues all global loads of its
-// first round of work (partial maxima, partial outputs, logits, ledger
-// entries) together before using any, so a unit costs about one dependent
-// L2 round trip plus the stores; larger units repeat rounds of four.
-template <int DT, typename Sync>
+// One combine unit of one (sequence, KV head) bh: the per-CTA partials'
+// maxima and sums give the head totals; with OUT, this unit's slice of the
+// output (each element the weighted sum of the partials in slot order --
+// main zone, then Q zone -- so results do not depend on timing, rounded the
+// way the reference rounds out_main, out_q and their sum, ops.py:150); with
+// FOLD, the exact probabilities of this unit's 64-token blocks folded into the
+// vote ledger / Q-window scores (tally_decode_scores, eviction_manager.py:198-203;
+// accumulate_scores, quantize_manager.py:101-111).  Run by nthr threads
+// (tid < nthr, nthr a multiple of 32 and >= 32*G) that synchronise with
+// sync(); N0 is the token count the attention pass saw (new token included).
+// Written for latency: a thread issues the global loads of its first round of
+// work (partial maxima, partial outputs, logits, ledger entries) together
+// before using any.
+template <int DT, bool OUT, bool FOLD, typename Sync>
 __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, void* __restrict__ out,
                                              const float* __restrict__ partial, const void* __restrict__ logits,
                                              const MmPlan& P, int N0, long long bh, int chunk, int nchunks,
                                              int blocks_per_chunk, float* sm, int tid, int nthr, Sync sync) {
     constexpr int MAXP = 64;
     constexpr int RW = 4;   // work items per thread per round
+    constexpr int XP = 16;  // partial outputs of one element loaded per round
     float(*s_m)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm);             // maxima, then weights
     float(*s_l)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm + MM_G * 128);
     float* s_M = sm + 2 * MM_G * 128;
     float* s_L = s_M + MM_G;
-    float(*s_acc)[MM_G * 128] = reinterpret_cast<float(*)[MM_G * 128]>(s_L + MM_G);
-    unsigned char* s_live = reinterpret_cast<unsigned char*>(s_L + MM_G + 2 * MM_G * 128);
+    unsigned char* s_live = reinterpret_cast<unsigned char*>(s_L + MM_G);
     using T = typename Elt<DT>::T;
     const int n_mblk = g.S_cap / 64;              // 64-token main blocks, then one per Q window
     const int n_blk = n_mblk + g.qw;
@@ -244,8 +248,6 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
     const int ne = G * 128;
     const int per = (ne + nchunks - 1) / nchunks;
     const int e0 = min(chunk * per, ne), e1 = min(e0 + per, ne);
-    const int ne_u = max(e1 - e0, 1);
-    const int work = (e1 - e0) * np;                  // (output element, partial) products, element fastest
     const int p_beg = blk0 * 64, p_end = min(blk1, n_mblk) * 64;
     const T* lg = reinterpret_cast<const T*>(logits) + (size_t)bh * S_tot * G;
     float* votes = L.votes + bh * g.S_cap;
@@ -260,35 +262,37 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
         pm = __ldcg(pr);
         pl = __ldcg(pr + 1);
     }
+    float xo[XP];
+    const int el_first = e0 + tid;
+    if (OUT && el_first < e1) {
+        const int hh = el_first >> 7, d = el_first & 127;
+#pragma unroll
+        for (int u = 0; u < XP; ++u) xo[u] = u < np ? __ldcg(prow(u) + hh * 130 + 2 + d) : 0.f;
+    }
     int32_t live_src = 1;
     const int sink_blk = g.sink / 64, ring_blk = (g.sink + g.kw * g.om) / 64;
     const int lb = blk0 + tid;
-    if (lb < blk1) {
-        if (lb >= sink_blk && lb < ring_blk) live_src = __ldcg(L.sticky_wid + bh * g.kw + (lb - sink_blk));
-        else if (lb >= n_mblk) live_src = __ldcg(L.q_wid + bh * g.qw + (lb - n_mblk));
-    }
-    float cv[RW];
-#pragma unroll
-    for (int u = 0; u < RW; ++u) {
-        const int t = tid + u * nthr;
-        cv[u] = 0.f;
-        if (t < work) cv[u] = __ldcg(prow(t / ne_u) + ((e0 + t % ne_u) >> 7) * 130 + 2 + ((e0 + t % ne_u) & 127));
-    }
     uint2 dl[RW];
     float dv[RW];
-#pragma unroll
-    for (int u = 0; u < RW; ++u) {
-        const int pos = p_beg + tid + u * nthr;
-        if (pos < p_end) {
-            dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
-            dv[u] = votes[pos];
-        }
-    }
     uint2 el2[2] = {make_uint2(0, 0), make_uint2(0, 0)};
-    if (G == 4 && q_blk < blk1) {
-        const T* wl = lg + ((size_t)g.S_cap + (size_t)(q_blk - n_mblk) * 64) * G;
-        el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
-        el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
+    if (FOLD) {
+        if (lb < blk1) {
+            if (lb >= sink_blk && lb < ring_blk) live_src = __ldcg(L.sticky_wid + bh * g.kw + (lb - sink_blk));
+            else if (lb >= n_mblk) live_src = __ldcg(L.q_wid + bh * g.qw + (lb - n_mblk));
+        }
+#pragma unroll
+        for (int u = 0; u < RW; ++u) {
+            const int pos = p_beg + tid + u * nthr;
+            if (pos < p_end) {
+                dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
+                dv[u] = votes[pos];
+            }
+        }
+        if (G == 4 && q_blk < blk1) {
+            const T* wl = lg + ((size_t)g.S_cap + (size_t)(q_blk - n_mblk) * 64) * G;
+            el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
+            el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
+        }
     }
     // ---- first uses: partial maxima / sums and the block liveness codes
     //      (0 = no live token, 1 = all live, 2 = live below offset tv)
@@ -296,19 +300,20 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
         s_m[am / np][am % np] = pm;
         s_l[am / np][am % np] = pl;
     }
-    for (int blk = lb; blk < blk1; blk += nthr) {
-        if (blk != lb) {   // units with more blocks than threads
-            live_src = 1;
-            if (blk >= sink_blk && blk < ring_blk) live_src = L.sticky_wid[bh * g.kw + (blk - sink_blk)];
-            else if (blk >= n_mblk) live_src = L.q_wid[bh * g.qw + (blk - n_mblk)];
+    if (FOLD) {
+        for (int blk = lb; blk < blk1; blk += nthr) {
+            if (blk != lb) {   // units with more blocks than threads
+                live_src = 1;
+                if (blk >= sink_blk && blk < ring_blk) live_src = L.sticky_wid[bh * g.kw + (blk - sink_blk)];
+                else if (blk >= n_mblk) live_src = L.q_wid[bh * g.qw + (blk - n_mblk)];
+            }
+            unsigned char code;
+            if (blk < sink_blk) code = 1;
+            else if (blk < ring_blk || blk >= n_mblk) code = live_src >= 0;
+            else code = mm_item_live(g, blk * 64 + 63, cw, 0) ? 1 : 2;
+            s_live[blk - blk0] = code;
         }
-        unsigned char code;
-        if (blk < sink_blk) code = 1;
-        else if (blk < ring_blk || blk >= n_mblk) code = live_src >= 0;
-        else code = mm_item_live(g, blk * 64 + 63, cw, 0) ? 1 : 2;
-        s_live[blk - blk0] = code;
     }
-    for (int t = tid; t < 2 * (e1 - e0); t += nthr) s_acc[t & 1][e0 + (t >> 1)] = 0.f;
     sync();
     // ---- (B) one warp per head: total maximum, normaliser, per-partial weights
     if (warp < G) {
@@ -327,73 +332,70 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
         if (lane == 0) { s_M[hh] = M; s_L[hh] = Ls; }
     }
     sync();
-    // ---- (C) output products, reduced in shared memory
-    for (int base = tid; base < work; base += RW * nthr) {
+    // ---- (C) output slice: every partial of an element added in slot order
+    if (OUT) {
+        const bool has_q = L.seq[b * 4 + 1] > 0;
+        for (int el = el_first; el < e1; el += nthr) {
+            const int hh = el >> 7, d = el & 127;
+            const float* w = s_m[hh];
+            float om_ = 0.f, oq = 0.f;
+            for (int base = 0; base < np; base += XP) {
+                if (base > 0 || el != el_first) {
 #pragma unroll
-        for (int u = 0; u < RW; ++u) {
-            const int t = base + u * nthr;
-            if (base != tid && t < work)
-                cv[u] = __ldcg(prow(t / ne_u) + ((e0 + t % ne_u) >> 7) * 130 + 2 + ((e0 + t % ne_u) & 127));
-        }
+                    for (int u = 0; u < XP; ++u) xo[u] = base + u < np ? __ldcg(prow(base + u) + hh * 130 + 2 + d) : 0.f;
+                }
 #pragma unroll
-        for (int u = 0; u < RW; ++u) {
-            const int t = base + u * nthr;
-            if (t < work) {
-                const int el = e0 + t % ne_u, s2 = t / ne_u;
-                atomicAdd(&s_acc[s2 < c0 ? 0 : 1][el], cv[u] * s_m[el >> 7][s2]);
+                for (int u = 0; u < XP; ++u) {
+                    const int s2 = base + u;
+                    if (s2 < c0) om_ = fmaf(xo[u], w[s2], om_);
+                    else if (s2 < np) oq = fmaf(xo[u], w[s2], oq);
+                }
             }
+            const float inv = 1.f / s_L[hh];
+            const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
+            st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
         }
     }
-    // ---- (D) main-zone tokens: exact probabilities into the vote ledger
-    for (int base = p_beg + tid; base < p_end; base += RW * nthr) {
-        if (base != p_beg + tid) {
+    if (FOLD) {
+        // ---- (D) main-zone tokens: exact probabilities into the vote ledger
+        for (int base = p_beg + tid; base < p_end; base += RW * nthr) {
+            if (base != p_beg + tid) {
+#pragma unroll
+                for (int u = 0; u < RW; ++u) {
+                    const int pos = base + u * nthr;
+                    if (pos < p_end) {
+                        dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
+                        dv[u] = votes[pos];
+                    }
+                }
+            }
 #pragma unroll
             for (int u = 0; u < RW; ++u) {
                 const int pos = base + u * nthr;
-                if (pos < p_end) {
-                    dl[u] = G == 4 ? __ldcg(reinterpret_cast<const uint2*>(lg + (size_t)pos * G)) : make_uint2(0, 0);
-                    dv[u] = votes[pos];
-                }
+                if (pos >= p_end) continue;
+                const int code = s_live[(pos >> 6) - blk0];
+                if (!(code == 1 || (code == 2 && (pos & 63) < tv))) continue;
+                const float acc = G == 4 ? group_prob_sum4<DT>(dl[u], s_M, s_L)
+                                         : group_prob_sum<DT>(lg + (size_t)pos * G, G, s_M, s_L);
+                votes[pos] = dv[u] + rnd<DT>(acc / (float)G);
             }
         }
-#pragma unroll
-        for (int u = 0; u < RW; ++u) {
-            const int pos = base + u * nthr;
-            if (pos >= p_end) continue;
-            const int code = s_live[(pos >> 6) - blk0];
-            if (!(code == 1 || (code == 2 && (pos & 63) < tv))) continue;
-            const float acc = G == 4 ? group_prob_sum4<DT>(dl[u], s_M, s_L)
-                                     : group_prob_sum<DT>(lg + (size_t)pos * G, G, s_M, s_L);
-            votes[pos] = dv[u] + rnd<DT>(acc / (float)G);
-        }
-    }
-    // ---- (E) Q windows: one warp per window, two tokens per lane
-    for (int blk = q_blk; blk < blk1; blk += nthr >> 5) {
-        const int slot = blk - n_mblk;
-        const T* wl = lg + ((size_t)g.S_cap + (size_t)slot * 64) * G;
-        if (blk != q_blk && G == 4) {
-            el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
-            el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
-        }
-        if (!s_live[blk - blk0]) continue;
-        const float a0 = G == 4 ? group_prob_sum4<DT>(el2[0], s_M, s_L)
-                                : group_prob_sum<DT>(wl + (size_t)lane * G, G, s_M, s_L);
-        const float a1 = G == 4 ? group_prob_sum4<DT>(el2[1], s_M, s_L)
-                                : group_prob_sum<DT>(wl + (size_t)(lane + 32) * G, G, s_M, s_L);
-        float a = rnd<DT>(a0 / (float)G) + rnd<DT>(a1 / (float)G);
-        a = warp_sum(a);
-        if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
-    }
-    sync();
-    // ---- output slice
-    {
-        const bool has_q = L.seq[b * 4 + 1] > 0;
-        for (int el = e0 + tid; el < e1; el += nthr) {
-            const int hh = el >> 7, d = el & 127;
-            const float inv = 1.f / s_L[hh];
-            const float om_ = s_acc[0][el], oq = s_acc[1][el];
-            const float r = has_q ? add_r<DT>(rnd<DT>(om_ * inv), rnd<DT>(oq * inv)) : rnd<DT>(om_ * inv);
-            st<DT>(out, ((size_t)b * g.H * G + (size_t)h * G + hh) * 128 + d, r);
+        // ---- (E) Q windows: one warp per window, two tokens per lane
+        for (int blk = q_blk; blk < blk1; blk += nthr >> 5) {
+            const int slot = blk - n_mblk;
+            const T* wl = lg + ((size_t)g.S_cap + (size_t)slot * 64) * G;
+            if (blk != q_blk && G == 4) {
+                el2[0] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)lane * G));
+                el2[1] = __ldcg(reinterpret_cast<const uint2*>(wl + (size_t)(lane + 32) * G));
+            }
+            if (!s_live[blk - blk0]) continue;
+            const float a0 = G == 4 ? group_prob_sum4<DT>(el2[0], s_M, s_L)
+                                    : group_prob_sum<DT>(wl + (size_t)lane * G, G, s_M, s_L);
+            const float a1 = G == 4 ? group_prob_sum4<DT>(el2[1], s_M, s_L)
+                                    : group_prob_sum<DT>(wl + (size_t)(lane + 32) * G, G, s_M, s_L);
+            float a = rnd<DT>(a0 / (float)G) + rnd<DT>(a1 / (float)G);
+            a = warp_sum(a);
+            if (lane == 0) L.q_score[bh * g.qw + slot] += rnd<DT>(a);
         }
     }
     sync();   // the scratch is reused by the next unit
@@ -470,17 +472,22 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             long long bh = i0 / P.ipb;
             int j = (int)(i0 % P.ipb) - 1;
 #pragma unroll 1
-            for (long long i = i0; i < i1; ++i) {
+            for (long long i = i0; i < i1; ++i, ++k) {
+                // item i takes stage slot k = i - i0 (round robin), fetched or not
                 if (++j == P.ipb) { j = 0; ++bh; }
-                if (skipped(i)) continue;
-                if (j == j_new && !waited) {
-                    asm volatile("griddepcontrol.wait;" ::: "memory");
-                    waited = true;
-                }
                 const int s = k % NS;
                 if (k >= NS && !mbar_wait_bounded(&empty[s], ((k / NS) - 1) & 1)) {
                     set_err(L.err, QV_DERR_LAYOUT);
                     break;
+                }
+                if (skipped(i)) {
+                    // no live token: the slot completes without a transfer
+                    mbar_arrive(&full[s]);
+                    continue;
+                }
+                if (j == j_new && !waited) {
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    waited = true;
                 }
                 unsigned char* st = stages + s * MM_STAGE;
                 if (j < P.n_main) {
@@ -500,7 +507,6 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
                     bulk_load(st + 16384 + 512, reinterpret_cast<const char*>(L.vs) + sw * 64 * e, 64 * e, &full[s]);
                     bulk_load(st + 16384 + 640, reinterpret_cast<const char*>(L.vz) + sw * 64 * e, 64 * e, &full[s]);
                 }
-                ++k;
             }
         }
         return;
@@ -512,9 +518,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
     uint32_t qq[8][2];            // the same q values in the Q-cache layout (see load_q)
     float o[8][4];                // O^T accumulators: 8 d-tiles x (2 rows x 2 heads)
     float m[2], ls[2], spp[2], svz[2];
-    int cur_key = -1;
     long long cur_bh = -1;
-    int k = 0;
     bool ok = true;
     T* lgp = reinterpret_cast<T*>(logits);
 
@@ -718,28 +722,25 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         ls[col] += sum;
     };
 
-    long long bh_it = i0 / P.ipb;
-    int j_it = (int)(i0 % P.ipb);
+    // Segment by segment (the items of one (sequence, head, zone) in this
+    // CTA's range): the warp group of this warp takes items i0 + grp,
+    // i0 + grp + NG, ...; item i is in stage slot (i - i0) mod NS.  Every
+    // warp closes every segment (flush), so the segment merge sees all warps.
+    constexpr int NG = CW / MM_SPLIT;
+    const int grp = warp / MM_SPLIT, part = warp % MM_SPLIT;
 #pragma unroll 1
-    for (long long i = i0;; ++i) {
-        const bool end = i >= i1;
-        const long long bh = bh_it;
-        const int j = j_it;
-        if (++j_it == P.ipb) { j_it = 0; ++bh_it; }
-        const int zone = j >= P.n_main ? 1 : 0;
-        const int key = end ? -2 : (int)(bh * 2 + zone);
-        if (key != cur_key) {
-            if (cur_key >= 0) flush(cur_key, end);
-            if (end) break;
-            if (bh != cur_bh) { load_q(bh); cur_bh = bh; }
-            reset_acc();
-            cur_key = key;
-        }
-        if (skipped(i)) continue;
-        const int kk_item = k++;
-        // items go round-robin to groups of MM_SPLIT warps; part = this warp's share
-        if (kk_item % (CW / MM_SPLIT) != warp / MM_SPLIT) continue;   // another group's item
-        const int part = warp % MM_SPLIT;
+    for (long long sa = i0; sa < i1;) {
+        const long long bh = sa / P.ipb;
+        const int zone = (int)(sa - bh * P.ipb) >= P.n_main ? 1 : 0;
+        const long long sb = min(i1, bh * P.ipb + (zone ? P.ipb : P.n_main));
+        if (bh != cur_bh) { load_q(bh); cur_bh = bh; }
+        reset_acc();
+        const long long rel = sa - i0;
+        const long long first = sa + (((long long)grp - rel) % NG + NG) % NG;
+#pragma unroll 1
+        for (long long i = first; i < sb; i += NG) {
+        const int j = (int)(i - bh * P.ipb);
+        const int kk_item = (int)(i - i0);
         const int s = kk_item % NS;
         // A warp that gives up waiting keeps walking the items (and joins every
         // named barrier) without computing, so no barrier is left unmatched.
@@ -747,7 +748,7 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
             set_err(L.err, QV_DERR_LAYOUT);
             ok = false;
         }
-        if (!ok) {
+        if (!ok || skipped(i)) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             continue;
@@ -958,6 +959,9 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        flush((int)(bh * 2 + zone), sb == i1);
+        sa = sb;
     }
     // let the combine grid get scheduled while this grid drains (it waits for
     // this grid's completion before reading anything).  Triggering at the
@@ -978,20 +982,21 @@ decode_mma_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant
 
 // Combine kernel: a grid of many small blocks, chained to the attention
 // kernel with programmatic dependent launch.  grid = (chunks, B*H).
-template <int DT>
+template <int DT, bool OUT, bool FOLD>
 __global__ void __launch_bounds__(256) decode_combine_kernel(Geo g, qv_layer L, void* __restrict__ out,
                                                              const float* __restrict__ partial,
                                                              const void* __restrict__ logits, MmPlan P,
                                                              int blocks_per_chunk) {
     __shared__ float sm[MM_CMB_SMEM];
-    // wait for the streaming kernel (programmatic dependent launch)
+    // wait for the streaming kernel (programmatic dependent launch; a no-op
+    // when launched after an event on another stream)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // a programmatic dependent (the output projection) may start streaming
     // its weights; it waits for this grid before reading the output
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int N0 = L.step[0] - 1;
-    combine_unit<DT>(g, L, out, partial, logits, P, N0, blockIdx.y, blockIdx.x, gridDim.x, blocks_per_chunk, sm,
-                     threadIdx.x, blockDim.x, BlockSync{});
+    combine_unit<DT, OUT, FOLD>(g, L, out, partial, logits, P, N0, blockIdx.y, blockIdx.x, gridDim.x,
+                                blocks_per_chunk, sm, threadIdx.x, blockDim.x, BlockSync{});
 }
 
 // ------------------------------------------------------------------ host side
@@ -1070,7 +1075,10 @@ size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
     return o;
 }
 
-int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s) {
+// mode: 0 = attention, output and ledger fold; 1 = attention and output (the
+// fold left pending); 2 = the pending fold of the attention launched last with
+// this workspace
+int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s, int mode) {
     MmPlan P = mm_plan(g);
     // a warp group may wait on a stage only one fill ahead of it: stages >= groups
     if (P.pmax > 64 || P.ns < P.cw / MM_SPLIT) return QV_EINVAL;
@@ -1081,12 +1089,14 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     const CUtensorMapDataType kt = g.dt == QV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint64_t rows = (uint64_t)g.B * g.H * g.S_cap;
     const uint64_t qrows = (uint64_t)g.B * g.H * (g.qw > 0 ? g.qw : 1) * 64;
-    bool okm = make_map(&mk, L.k, kt, 128, rows, 256, 64, MM_MT) && make_map(&mv, L.v, kt, 128, rows, 256, 64, MM_MT);
-    const void* kqb = g.qw > 0 ? (const void*)L.kq : (const void*)L.k;
-    const void* vqb = g.qw > 0 ? (const void*)L.vq : (const void*)L.v;
-    okm = okm && make_map(&mkq, kqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64) &&
-          make_map(&mvq, vqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64);
-    if (!okm) return QV_EINVAL;
+    if (mode != 2) {
+        bool okm = make_map(&mk, L.k, kt, 128, rows, 256, 64, MM_MT) && make_map(&mv, L.v, kt, 128, rows, 256, 64, MM_MT);
+        const void* kqb = g.qw > 0 ? (const void*)L.kq : (const void*)L.k;
+        const void* vqb = g.qw > 0 ? (const void*)L.vq : (const void*)L.v;
+        okm = okm && make_map(&mkq, kqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64) &&
+              make_map(&mvq, vqb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, qrows, 128, 128, 64);
+        if (!okm) return QV_EINVAL;
+    }
     const size_t smem = mm_fixed_smem(g, P.cw) + (size_t)P.ns * MM_STAGE;
     static int cached[2][2] = {{48 * 1024, 48 * 1024}, {48 * 1024, 48 * 1024}};
     int* tickets = reinterpret_cast<int*>(base);
@@ -1117,11 +1127,17 @@ int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* w
     const bool wide = P.cw == MM_CW_WIDE;
     auto kern = g.dt == QV_BF16 ? (wide ? decode_mma_kernel<QV_BF16, MM_CW_WIDE> : decode_mma_kernel<QV_BF16, MM_CW_NARROW>)
                                 : (wide ? decode_mma_kernel<QV_F16, MM_CW_WIDE> : decode_mma_kernel<QV_F16, MM_CW_NARROW>);
-    auto comb = g.dt == QV_BF16 ? decode_combine_kernel<QV_BF16> : decode_combine_kernel<QV_F16>;
-    cudaError_t e = ensure_smem(kern, smem, &cached[g.dt == QV_BF16 ? 0 : 1][wide ? 1 : 0]);
-    if (e != cudaSuccess) return set_cuda_error(e);
-    e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
-    if (e != cudaSuccess) return set_cuda_error(e);
+    const bool bf = g.dt == QV_BF16;
+    auto comb = mode == 0 ? (bf ? decode_combine_kernel<QV_BF16, true, true> : decode_combine_kernel<QV_F16, true, true>)
+              : mode == 1 ? (bf ? decode_combine_kernel<QV_BF16, true, false> : decode_combine_kernel<QV_F16, true, false>)
+                          : (bf ? decode_combine_kernel<QV_BF16, false, true> : decode_combine_kernel<QV_F16, false, true>);
+    cudaError_t e = cudaSuccess;
+    if (mode != 2) {
+        e = ensure_smem(kern, smem, &cached[bf ? 0 : 1][wide ? 1 : 0]);
+        if (e != cudaSuccess) return set_cuda_error(e);
+        e = cudaLaunchKernelEx(&cfg1, kern, mk, mv, mkq, mvq, g, L, q, tickets, part, lgt, P);
+        if (e != cudaSuccess) return set_cuda_error(e);
+    }
     e = cudaLaunchKernelEx(&cfg2, comb, g, L, out, (const float*)part, (const void*)lgt, P, bpc);
     if (e != cudaSuccess) return set_cuda_error(e);
     return check_launch();

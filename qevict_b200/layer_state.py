@@ -154,10 +154,19 @@ class StickyLayerState:
                    N.ptr(cos), N.ptr(sin), N.ptr(self.q_rot), self._stream())
         return self.q_rot
 
-    def attend(self, q_rot, out):
-        self._call("qv_decode_attention", ctypes.byref(self.dims), ctypes.byref(self.layer),
+    def attend(self, q_rot, out, fold=True):
+        """Fused attention of the token appended last; fold=False leaves the
+        vote-ledger fold pending for fold() (qv_decode_attention_nofold)."""
+        name = "qv_decode_attention" if fold else "qv_decode_attention_nofold"
+        self._call(name, ctypes.byref(self.dims), ctypes.byref(self.layer),
                    N.ptr(q_rot), N.ptr(out), N.ptr(self.ws.decode), self.ws.decode_bytes, self._stream())
         self.n_tokens += 1
+
+    def fold(self):
+        """The ledger fold left pending by attend(..., fold=False) (qv_decode_fold), on
+        the current stream; it must run before the next append / attend / cycle."""
+        self._call("qv_decode_fold", ctypes.byref(self.dims), ctypes.byref(self.layer),
+                   N.ptr(self.ws.decode), self.ws.decode_bytes, self._stream())
 
     def evict_cycle(self):
         self._call("qv_evict_cycle", ctypes.byref(self.dims), ctypes.byref(self.layer),

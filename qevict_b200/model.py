@@ -14,7 +14,13 @@ around the prefill lane (causal attention + column sums -> state build).
 
 Decode steps are captured in two CUDA graphs (a plain step and a step that
 ends an omega-window and runs the eviction cycle of every layer); all
-per-step indices live on the device, so the graphs replay unchanged.
+per-step indices live on the device, so the graphs replay unchanged.  With
+side_fold, a plain step runs each layer's vote-ledger fold on a side stream
+beside the layer's projections (the ledger only feeds the next eviction cycle)
+and joins it at the step's end; each layer then has its own decode workspace.
+A cycle step folds inline, since the cycle reads the ledger.  The default
+folds inline: on a B200 the full-model step measured 3.74 ms inline against
+3.81 ms with the side stream (batch 1, 32k context).
 """
 
 import math
@@ -90,7 +96,7 @@ class StickyLlamaDecoder:
     """Random-init Llama decoder, batch B, with Sticky-KV attention in every layer."""
 
     def __init__(self, shape: LlamaShape, sticky: StickyShape, batch=1, max_pos=40960,
-                 dtype=torch.bfloat16, device="cuda", seed=0, std=0.02):
+                 dtype=torch.bfloat16, device="cuda", seed=0, std=0.02, side_fold=False):
         self.s, self.k, self.B = shape, sticky, batch
         self.dtype, self.device = dtype, torch.device(device)
         g = torch.Generator(device=self.device)
@@ -117,14 +123,15 @@ class StickyLlamaDecoder:
         self.max_pos = max_pos
         max_windows = max((max_pos - sticky.sink) // sticky.omega, 100)
         self.states = []
+        self.side_fold = side_fold
         ws = None
         for _ in range(s.layers):
             st = StickyLayerState(batch, H, Hq // H, D, sticky.omega, sticky.sink, sticky.local,
                                   sticky.k_windows, sticky.q_windows, max_windows, sticky.bits, dtype,
-                                  self.device, workspace=ws)
+                                  self.device, workspace=None if side_fold else ws)
             ws = st.ws
             self.states.append(st)
-        self.ws = ws
+        self.fold_stream = torch.cuda.Stream(device=self.device) if side_fold else None
         # static decode buffers (graph inputs/outputs)
         self.tok = torch.zeros(batch, dtype=torch.long, device=self.device)
         self.next_tok = torch.zeros(batch, dtype=torch.long, device=self.device)
@@ -192,7 +199,7 @@ class StickyLlamaDecoder:
                              torch.cuda.current_stream(self.device).cuda_stream)
         N.check(rc, "qv_gemv")
 
-    def _layer_step(self, li):
+    def _layer_step(self, li, cycle=False):
         """One decoder layer on self.x; expects self.h = RMSNorm(x) * ln1 and leaves
         self.h = RMSNorm(x_out) * (the next layer's ln1, or the final norm)."""
         s, L, st = self.s, self.layers[li], self.states[li]
@@ -203,7 +210,14 @@ class StickyLlamaDecoder:
         k = self.qkv[:, Hq * D:(Hq + H) * D].view(B, H, D)
         v = self.qkv[:, (Hq + H) * D:].view(B, H, D)
         qr = st.append(q, k, v, self.cos, self.sin)
-        st.attend(qr, self.attn_out)
+        if cycle or not self.side_fold:
+            st.attend(qr, self.attn_out)
+        else:
+            # the ledger fold goes to the side stream, beside the projections below
+            st.attend(qr, self.attn_out, fold=False)
+            self.fold_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.fold_stream):
+                st.fold()
         self._gemv(L["wo"], self.attn_out, self.proj)
         self._add_norm(self.proj, L["ln2"])
         self._gemv(L["wgu"], self.h, self.gu)
@@ -218,7 +232,7 @@ class StickyLlamaDecoder:
         torch.index_select(self.embed, 0, self.tok, out=self.x)
         self._add_norm(None, self.layers[0]["ln1"])
         for li in range(self.s.layers):
-            self._layer_step(li)
+            self._layer_step(li, cycle)
             if cycle:
                 self.states[li].evict_cycle()
         self._gemv(self.lm_head, self.h, self.logits)
@@ -226,6 +240,9 @@ class StickyLlamaDecoder:
                                self.argmax_ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
         N.check(rc, "qv_argmax")
         self.tok.copy_(self.next_tok)
+        if self.side_fold and not cycle:
+            # join the side stream's ledger folds
+            torch.cuda.current_stream(self.device).wait_stream(self.fold_stream)
 
     def cycle_next(self):
         """Whether the next decode token completes an omega-window."""

@@ -442,3 +442,44 @@ def test_misaligned_prompt_rejected():
     k = torch.zeros(1, 2, 64 + 64 * 5 + 7, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(QevictError):
         st.prefill(k, k, torch.zeros(1, 2, k.shape[2], device="cuda"))
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp32"])
+def test_deferred_fold_matches_inline(dt):
+    """qv_decode_attention_nofold + qv_decode_fold (the fold run later, here on a
+    second stream after an event) give the same outputs, vote ledgers and
+    Q-window scores as qv_decode_attention, bit for bit, through cycles.  bf16
+    takes the tensor-core kernel (separate output and fold launches), fp32 the
+    CUDA-core kernel (the fold inside the attention launch)."""
+    from qevict_b200 import StickyLayerState
+    B, H, G, D, om, sink, local, kw, qw = 2, 2, 4, 128, 64, 64, 128, 3, 4
+    g = torch.Generator(device="cuda").manual_seed(4)
+    S = sink + 10 * om
+    k = torch.randn(B, H, S, D, generator=g, device="cuda").to(TD[dt])
+    v = torch.randn(B, H, S, D, generator=g, device="cuda").to(TD[dt])
+    cs = torch.rand(B, H, S, generator=g, device="cuda") * 4
+    a = StickyLayerState(B, H, G, D, om, sink, local, kw, qw, 64, 8, TD[dt])
+    b = StickyLayerState(B, H, G, D, om, sink, local, kw, qw, 64, 8, TD[dt])
+    a.prefill(k, v, cs)
+    b.prefill(k, v, cs)
+    side = torch.cuda.Stream()
+    oa = torch.empty(B, H * G, D, dtype=TD[dt], device="cuda")
+    ob = torch.empty_like(oa)
+    for step in range(2 * om + 3):
+        q = (torch.randn(B, H * G, D, generator=g, device="cuda") * 0.5).to(TD[dt])
+        kn = torch.randn(B, H, D, generator=g, device="cuda").to(TD[dt])
+        vn = torch.randn(B, H, D, generator=g, device="cuda").to(TD[dt])
+        a.attend(a.append(q, kn, vn), oa)
+        b.attend(b.append(q, kn, vn), ob, fold=False)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            b.fold()
+        torch.cuda.current_stream().wait_stream(side)
+        assert torch.equal(oa, ob), f"step {step}: outputs differ"
+        assert torch.equal(a.votes, b.votes), f"step {step}: ledgers differ"
+        assert torch.equal(a.q_score, b.q_score), f"step {step}: Q-window scores differ"
+        if a.cycle_due():
+            a.evict_cycle()
+            b.evict_cycle()
+            assert torch.equal(a.sticky_wid, b.sticky_wid) and torch.equal(a.q_wid, b.q_wid)
+    assert a.read_error() == 0 and b.read_error() == 0

@@ -50,13 +50,16 @@ def test_silu_mul():
     assert bool((err <= ref.abs() * 2.0 ** -7 + 1e-6).all())
 
 
-def test_small_decoder_graph_matches_eager():
+@pytest.mark.parametrize("side_fold", [False, True])
+def test_small_decoder_graph_matches_eager(side_fold):
+    """The captured step equals the eager step token for token, with the ledger
+    fold inline and with it on the side stream."""
     from qevict_b200.model import LlamaShape, StickyLlamaDecoder, StickyShape
     shape = LlamaShape(vocab=1000, hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512)
     sticky = StickyShape(omega=16, sink=16, local=32, k_windows=3, q_windows=4, bits=8)
     toks = []
     for mode in ("eager", "graph"):
-        m = StickyLlamaDecoder(shape, sticky, batch=2, max_pos=1024, seed=7, std=0.05)
+        m = StickyLlamaDecoder(shape, sticky, batch=2, max_pos=1024, seed=7, std=0.05, side_fold=side_fold)
         ids = torch.randint(0, shape.vocab, (2, 16 + 8 * 16), generator=torch.Generator().manual_seed(1)).cuda()
         m.prefill(ids)
         if mode == "graph":
