@@ -53,6 +53,7 @@ enum {
     QV_DERR_TABLE = 1 << 0,    /* window id outside [0, max_windows) */
     QV_DERR_LAYOUT = 1 << 1,   /* a window was not found where the layout says it is */
     QV_DERR_CAPACITY = 1 << 2, /* more movers than free slots */
+    QV_DERR_TIMEOUT = 1 << 3,  /* a bounded wait of a pipelined kernel gave up (the output is not valid) */
 };
 
 typedef struct qv_dims {
@@ -235,11 +236,19 @@ int qv_prefill_build(const qv_dims* d, const qv_layer* L, const void* k_prompt, 
  * GQA-group-mean softmax (512-query chunks rounded to the kv dtype, fp32
  * across chunks).  Replaces flash_attn_func + compute_chunked_prefill_scores
  * (src/models/attention/ops_flash.py:22-141).
- * q [B][S][G*H][D], k,v [B][S][H][D] (rotated); out [B][S][G*H][D]; colsum [B][H][S] fp32. */
+ * q [B][S][G*H][D], k,v [B][S][H][D] (rotated); out [B][S][G*H][D]; colsum [B][H][S] fp32.
+ * Workspace (qv_prefill_workspace_bytes): per-row softmax statistics, and for
+ * bf16/fp16 the column-sum partials, a triangle of about S*S*G/256 fp32 values
+ * per sequence and KV head (0.54 GB for 8 KV heads, G = 4, S = 32768). */
 int qv_prefill_attention(const qv_dims* d, const void* q, const void* k, const void* v, int32_t seq_len,
                          void* out, float* colsum, void* workspace, size_t workspace_bytes,
                          qv_stream_t stream);
 size_t qv_prefill_workspace_bytes(const qv_dims* d, int32_t seq_len);
+/* The device error word of the last qv_prefill_attention on this workspace
+ * (0, or QV_DERR_TIMEOUT when a pipelined kernel gave up waiting and its
+ * outputs are not valid); pass the workspace and size given to
+ * qv_prefill_attention.  Synchronises the stream. */
+int qv_prefill_read_error(const void* workspace, size_t workspace_bytes, int32_t* host_err, qv_stream_t stream);
 
 /* ---- codec (the reference's static methods) ----------------------------- */
 

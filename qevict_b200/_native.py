@@ -12,7 +12,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "li
 
 QV_OK, QV_EINVAL, QV_ENOTALIGNED, QV_ESPACE, QV_ECUDA = 0, -1, -2, -3, -4
 QV_F32, QV_BF16, QV_F16 = 0, 1, 2
-QV_DERR_TABLE, QV_DERR_LAYOUT, QV_DERR_CAPACITY = 1, 2, 4
+QV_DERR_TABLE, QV_DERR_LAYOUT, QV_DERR_CAPACITY, QV_DERR_TIMEOUT = 1, 2, 4, 8
 QV_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024   # include/qevict_b200.h
 
 _ERRNAMES = {QV_EINVAL: "invalid argument", QV_ENOTALIGNED: "prompt/local zone not window-aligned",
@@ -73,6 +73,7 @@ def lib():
         "qv_prefill_build": (ctypes.c_int, [D, Lp, vp, vp, i32, vp, i32, vp]),
         "qv_prefill_attention": (ctypes.c_int, [D, vp, vp, vp, i32, vp, vp, vp, sz, vp]),
         "qv_prefill_workspace_bytes": (sz, [D, i32]),
+        "qv_prefill_read_error": (ctypes.c_int, [vp, sz, P(i32), vp]),
         "qv_quantize_k": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
         "qv_quantize_v": (ctypes.c_int, [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
         "qv_dequantize": (ctypes.c_int, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
@@ -103,7 +104,7 @@ def exported_symbols():
             "qv_cycle_workspace_bytes", "qv_rope_append", "qv_rope", "qv_decode_attention",
             "qv_decode_attention_noalloc", "qv_decode_attention_nofold", "qv_decode_fold", "qv_evict_cycle",
             "qv_evict_cycle_count", "qv_evict_cycle_ext",
-            "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes",
+            "qv_prefill_build", "qv_prefill_attention", "qv_prefill_workspace_bytes", "qv_prefill_read_error",
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_gemv",
             "qv_argmax_workspace_bytes", "qv_argmax", "qv_track_prefill", "qv_track_decode",
             "qv_track_positions", "qv_read_error",

@@ -242,8 +242,9 @@ prefill_colsum_kernel(Geo g, const void* __restrict__ q, const void* __restrict_
 
 // tensor-core prefill lane (prefill_tc.cu) for bf16/fp16
 bool pft_supported(const Geo& g);
+size_t pft_partial_bytes(const Geo& g, int S);
 int pft_launch(const Geo& g, const void* q, const void* k, const void* v, int S, void* out, float* colsum,
-               float* stats, int* err, cudaStream_t s);
+               float* stats, float* partial, int* err, cudaStream_t s);
 
 static size_t fwd_smem(int D) { return (size_t)(2 * PT * (D + 1) + PT * D + PT * (PT + 1) + PT) * 4; }
 static size_t col_smem(int D) { return (size_t)(2 * PT * (D + 1) + 2 * PT + 16 * PT + 2 * PT) * 4; }
@@ -270,9 +271,34 @@ static int launch_prefill(const Geo& g, const void* q, const void* k, const void
 
 using namespace qv;
 
+// Workspace: the per-row softmax statistics; for the tensor-core lane the
+// column-sum partials; then the device error word of the pipelined lane, at
+// the last 256-byte boundary at least 256 bytes before the workspace's end.
+static size_t err_offset(size_t workspace_bytes) { return (workspace_bytes - 256) & ~(size_t)255; }
+
+static size_t stats_bytes(const qv_dims* d, int32_t S) {
+    const size_t n = (size_t)d->batch * d->kv_heads * d->group * (size_t)S * 2 * sizeof(float);
+    return (n + 255) & ~(size_t)255;
+}
+
+static size_t partial_bytes(const qv_dims* d, int32_t S) {
+    const Geo g = make_geo(d);
+    if (!pft_supported(g)) return 0;
+    return (pft_partial_bytes(g, S) + 255) & ~(size_t)255;
+}
+
 extern "C" size_t qv_prefill_workspace_bytes(const qv_dims* d, int32_t S) {
     if (!d || S <= 0) return 0;
-    return (size_t)d->batch * d->kv_heads * d->group * (size_t)S * 2 * sizeof(float);
+    return stats_bytes(d, S) + partial_bytes(d, S) + 256;
+}
+
+extern "C" int qv_prefill_read_error(const void* workspace, size_t workspace_bytes, int32_t* host_err,
+                                     qv_stream_t stream) {
+    if (!workspace || !host_err || workspace_bytes < 256) return QV_EINVAL;
+    const int32_t* err = reinterpret_cast<const int32_t*>(static_cast<const char*>(workspace) + err_offset(workspace_bytes));
+    cudaError_t e = cudaMemcpyAsync(host_err, err, sizeof(int32_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    return e == cudaSuccess ? QV_OK : set_cuda_error(e);
 }
 
 extern "C" int qv_prefill_attention(const qv_dims* d, const void* q, const void* k, const void* v, int32_t S,
@@ -284,8 +310,14 @@ extern "C" int qv_prefill_attention(const qv_dims* d, const void* q, const void*
     if (workspace_bytes < qv_prefill_workspace_bytes(d, S) || !workspace) return QV_ESPACE;
     Geo g = make_geo(d);
     float* stats = reinterpret_cast<float*>(workspace);
+    int* err = reinterpret_cast<int*>(static_cast<char*>(workspace) + err_offset(workspace_bytes));
     cudaStream_t s = (cudaStream_t)stream;
-    if (pft_supported(g)) return pft_launch(g, q, k, v, S, out, colsum, stats, nullptr, s);
+    cudaError_t ce = cudaMemsetAsync(err, 0, sizeof(int), s);
+    if (ce != cudaSuccess) return set_cuda_error(ce);
+    if (pft_supported(g)) {
+        float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + stats_bytes(d, S));
+        return pft_launch(g, q, k, v, S, out, colsum, stats, partial, err, s);
+    }
 #define QV_PA(DT)                                                                   \
     return g.D == 128 ? launch_prefill<DT, 128>(g, q, k, v, S, out, colsum, stats, s) \
                       : launch_prefill<DT, 64>(g, q, k, v, S, out, colsum, stats, s)

@@ -4,27 +4,42 @@
 // fp32): causal attention output and the per-key column sums the reference's
 // chunked scorer produces (src/models/attention/ops_flash.py:56-141):
 // logits rounded like the reference (q.k rounded to the KV dtype, / sqrt(D)
-// rounded), fp32 softmax statistics per query row, probabilities rounded to the
-// KV dtype, group mean rounded, sums over each 512-query chunk rounded, chunks
-// accumulated in fp32.
+// rounded, src/models/attention/ops.py:23-46), fp32 softmax statistics per
+// query row, probabilities rounded to the KV dtype, group mean rounded, sums
+// over each 512-query chunk rounded, chunks accumulated in fp32.
 //
-// Three kernels, each a 128-thread CTA (four warps = the four TMEM lane
-// quarters, one thread per tile row); thread 0 issues the TMA loads and the
-// tcgen05.mma instructions and commits them to mbarriers; every wait is
-// bounded.  Operand tiles are 4-D TMA boxes (64 elements x rows) with the
-// 128-byte swizzle, which is the canonical K-major / MN-major UMMA layout.
+// Warp-specialised kernels.  Each tile CTA has ten warps: eight compute warps
+// (two per TMEM lane quarter, each owning half of a tile's 128 columns), one
+// TMA warp and one MMA warp (one elected thread each).  The score tile S is
+// double-buffered in TMEM, so the tensor cores compute tile j+1 while the
+// compute warps round, exponentiate and reduce tile j; operands stream through
+// multi-stage shared-memory rings guarded by mbarriers.  Every wait is bounded
+// and also gives up at once when another CTA has raised the error word.
+// Operand tiles are 4-D TMA boxes (64 elements x rows) with the 128-byte
+// swizzle, the canonical K-major / MN-major UMMA layout.
 //
 //   pft_stats_kernel   one CTA per (128-query tile, query head): S = Q.K^T per
-//                      128-key tile into TMEM (M = queries, N = keys), running
-//                      max / sum of exp of the rounded logits per row.
-//   pft_out_kernel     the same S tiles; P = exp(l - max) / sum rounded to the
-//                      KV dtype is written to shared memory (swizzled) and
-//                      O += P.V runs on the tensor cores (V as an MN-major
-//                      operand), O accumulating in TMEM across key tiles.
-//   pft_colsum_kernel  one CTA per (128-key tile, KV head): S^T = K.Q^T with
-//                      the keys in M and (query, group head) pairs in N
-//                      (32 queries x G heads), so each thread owns one key and
-//                      folds the group mean and the chunk sums on its own.
+//                      128-key tile (M = queries, N = keys); running max and
+//                      sum of exp of the rounded logits per row -> (max,
+//                      1 / sum) in the stats buffer [B][H][S][G][2].
+//   pft_attn_kernel    one CTA per (block of 128 / G queries, KV head), rows =
+//                      (query, group head): the same S tiles; P rounded to the
+//                      KV dtype in shared memory; O += P.V and the group sums
+//                      P^T.W on the tensor cores; per (query block, key) the
+//                      sum of the rounded group means -> partials.
+//   pft_chunk_kernel   per key: the partials of each 512-query chunk summed and
+//                      rounded, chunks accumulated in fp32 -> column sums.
+//
+// Arithmetic the compute warps rely on:
+// * the division by sqrt(D) is a multiply by the fp32 reciprocal: for every
+//   bf16 input (and every fp16 input at D = 64) round(round(x) * (1/sqrt(D)))
+//   equals round(round(x) / sqrt(D)) exactly; fp16 at D = 128 adds one
+//   residual correction (q' = q + (x - q*sqrt(D)) / sqrt(D), two FMAs), which
+//   makes it equal in value for all 65536 inputs.  tests/test_prefill_rounding.py
+//   checks both identities over every 16-bit input;
+// * exp(x) is ex2.approx(x * log2(e)) on x = l - max (exact: both are values
+//   of the KV dtype); its few-ulp fp32 error only moves a probability across
+//   a rounding boundary of the KV dtype, which the lane's parity bounds allow.
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -36,21 +51,37 @@ namespace qv {
 
 constexpr int PFT_ROWS = 128;        // queries (stats/out) or keys (colsum) per tile
 constexpr int PFT_SLAB = 16384;      // one 64-element x 128-row swizzled slab
-constexpr int PFT_QB = 32;           // queries per colsum step
 constexpr int PFT_CHUNK = 512;       // queries per rounded chunk of the scorer
+constexpr int PFT_CW = 8;            // compute warps
+constexpr int PFT_TMA_WARP = PFT_CW;
+constexpr int PFT_MMA_WARP = PFT_CW + 1;
+constexpr int PFT_THREADS = 32 * (PFT_CW + 2);
+constexpr float PFT_LOG2E = 1.4426950408889634f;
 
 struct PftArgs {
     int S, B, H, G, Hq;
-    float* stats;                    // [B][Hq][S][2]: max, sum
+    float* stats;                    // [B][H][S][G][2]: max, 1 / sum
     void* out;                       // [B][S][Hq][D]
-    float* colsum;                   // [B][H][S]
-    int* err;                        // set to 1 when a wait gives up
+    float* partial;                  // [B][H] x triangle: query block j holds keys [0, (j+1) * QB)
+    int* err;                        // device error word (QV_DERR_TIMEOUT)
 };
 
+// Bounded wait: false after about a second (raising the error word), or at
+// once when another CTA has raised it.
+__device__ __noinline__ bool pft_wait_slow(uint64_t* bar, uint32_t parity, int* err) {
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+        if (global_ns() - t0 > 1000000000ull) {
+            atomicOr(err, QV_DERR_TIMEOUT);
+            return false;
+        }
+    }
+}
 __device__ __forceinline__ bool pft_wait(uint64_t* bar, uint32_t parity, int* err) {
-    if (mbar_wait_bounded(bar, parity)) return true;
-    if (err) atomicExch(err, 1);
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    return pft_wait_slow(bar, parity, err);
 }
 
 template <int D>
@@ -59,374 +90,483 @@ __device__ __forceinline__ uint32_t pft_kmajor_step(uint32_t base, int kk) {
     return base + (uint32_t)((kk >> 2) * PFT_SLAB + (kk & 3) * 32);
 }
 
+__device__ __forceinline__ float pft_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void pft_named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Two fp32 values rounded to the KV dtype (one packed conversion), and back.
+template <int DT> __device__ __forceinline__ uint32_t pft_pack(float hi, float lo) {
+    uint32_t p;
+    if (DT == QV_BF16)
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+    else
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+    return p;
+}
+template <int DT> __device__ __forceinline__ void pft_unpack(uint32_t p, float& hi, float& lo) {
+    if (DT == QV_BF16) {
+        hi = __uint_as_float(p & 0xFFFF0000u);
+        lo = __uint_as_float(p << 16);
+    } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&p);
+        hi = __high2float(h);
+        lo = __low2float(h);
+    }
+}
+
+// The reference's logit of an fp32 accumulator pair: round(round(x) / sqrt(D)).
+template <int DT, int D> __device__ __forceinline__ void pft_logit2(float& a, float& b, float inv, float sd) {
+    float ra, rb;
+    pft_unpack<DT>(pft_pack<DT>(a, b), ra, rb);
+    float qa = __fmul_rn(ra, inv), qb = __fmul_rn(rb, inv);
+    if (DT == QV_F16 && D != 64) {
+        qa = __fmaf_rn(__fmaf_rn(-qa, sd, ra), inv, qa);
+        qb = __fmaf_rn(__fmaf_rn(-qb, sd, rb), inv, qb);
+    }
+    pft_unpack<DT>(pft_pack<DT>(qa, qb), a, b);
+}
+
 // ---------------------------------------------------------------- stats
 template <int DT, int D>
-__global__ void __launch_bounds__(128, 1) pft_stats_kernel(const __grid_constant__ CUtensorMap mQ,
-                                                           const __grid_constant__ CUtensorMap mK, PftArgs a) {
+__global__ void __launch_bounds__(PFT_THREADS, 1) pft_stats_kernel(const __grid_constant__ CUtensorMap mQ,
+                                                                   const __grid_constant__ CUtensorMap mK, PftArgs a) {
     constexpr int NS = D / 64;                   // slabs per operand tile
+    constexpr int KST = 3;                       // K stages
     extern __shared__ unsigned char pft_raw[];
     unsigned char* sm = pft_raw + ((1024u - (smem_u32(pft_raw) & 1023u)) & 1023u);
-    unsigned char* sQ = sm;                      // [NS] slabs
-    unsigned char* sK = sm + NS * PFT_SLAB;      // [2][NS] slabs
-    __shared__ __align__(8) uint64_t bar_k[2], bar_s;
+    unsigned char* sQ = sm;                      // [NS]
+    unsigned char* sK = sm + NS * PFT_SLAB;      // [KST][NS]
+    __shared__ __align__(8) uint64_t bar_q, kfull[KST], kempty[KST], sfull[2], sempty[2], done;
+    __shared__ float red[PFT_ROWS][2];
     __shared__ uint32_t s_taddr;
-    const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+    const int qt = gridDim.x - 1 - blockIdx.x;   // longest rows first
+    const int hq = blockIdx.y, b = blockIdx.z;
     const int h = hq / a.G;
-    const int warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q0 = qt * PFT_ROWS;
     const int nkt = qt + 1;
-    const float sqrt_d = sqrtf((float)D);
+    int* err = a.err;
 
-    if (warp == 0) { tmem_alloc(&s_taddr, 128); tmem_relinquish(); }
+    if (warp == PFT_MMA_WARP) { tmem_alloc(&s_taddr, 256); tmem_relinquish(); }
     if (threadIdx.x == 0) {
-        mbar_init(&bar_k[0], 1); mbar_init(&bar_k[1], 1); mbar_init(&bar_s, 1);
+        mbar_init(&bar_q, 1);
+        for (int s = 0; s < KST; ++s) { mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&sfull[s], 1); mbar_init(&sempty[s], PFT_CW); }
+        mbar_init(&done, 1);
         fence_barrier_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t taddr = s_taddr;
-    const uint32_t idesc = umma_idesc_f16(DT == QV_BF16, 128, 128, 0, 0);
-    if (threadIdx.x == 0) {
-        prefetch_tensormap(&mQ);
-        prefetch_tensormap(&mK);
-        mbar_arrive_expect_tx(&bar_k[0], 2 * NS * PFT_SLAB);
-        for (int s = 0; s < NS; ++s) {
-            tma_load_4d(sQ + s * PFT_SLAB, &mQ, 64 * s, hq, q0, b, &bar_k[0]);
-            tma_load_4d(sK + s * PFT_SLAB, &mK, 64 * s, h, 0, b, &bar_k[0]);
-        }
-    }
-    const int qi = q0 + threadIdx.x;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int kt = 0; kt < nkt; ++kt) {
-        const int st = kt & 1;
-        if (threadIdx.x == 0) {
-            if (kt + 1 < nkt) {
-                mbar_arrive_expect_tx(&bar_k[st ^ 1], NS * PFT_SLAB);
+
+    if (warp == PFT_TMA_WARP) {
+        if (lane == 0) {
+            prefetch_tensormap(&mQ);
+            prefetch_tensormap(&mK);
+            mbar_arrive_expect_tx(&bar_q, NS * PFT_SLAB);
+            for (int s = 0; s < NS; ++s) tma_load_4d(sQ + s * PFT_SLAB, &mQ, 64 * s, hq, q0, b, &bar_q);
+            int issued = 0;
+            bool ok = true;
+            for (int kt = 0; kt < nkt; ++kt) {
+                const int st = kt % KST;
+                if (kt >= KST) ok = ok && pft_wait(&kempty[st], (kt / KST - 1) & 1, err);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&kfull[st], NS * PFT_SLAB);
                 for (int s = 0; s < NS; ++s)
-                    tma_load_4d(sK + ((st ^ 1) * NS + s) * PFT_SLAB, &mK, 64 * s, h, (kt + 1) * PFT_ROWS, b, &bar_k[st ^ 1]);
+                    tma_load_4d(sK + (st * NS + s) * PFT_SLAB, &mK, 64 * s, h, kt * PFT_ROWS, b, &kfull[st]);
+                issued = kt + 1;
             }
-            if (pft_wait(&bar_k[st], (kt >> 1) & 1, a.err)) {
+            // the copies this thread issued have landed before the CTA exits
+            mbar_wait_bounded(&bar_q, 0);
+            for (int kt = issued - KST > 0 ? issued - KST : 0; kt < issued; ++kt)
+                mbar_wait_bounded(&kfull[kt % KST], (kt / KST) & 1);
+        }
+    } else if (warp == PFT_MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(DT == QV_BF16, 128, 128, 0, 0);
+            bool ok = pft_wait(&bar_q, 0, err);
+            for (int kt = 0; kt < nkt && ok; ++kt) {
+                const int st = kt % KST, bf = kt & 1;
+                ok = pft_wait(&kfull[st], (kt / KST) & 1, err);
+                if (ok && kt >= 2) ok = pft_wait(&sempty[bf], ((kt >> 1) - 1) & 1, err);
+                if (!ok) break;
                 tc_fence_after();
                 const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + st * NS * PFT_SLAB);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(taddr, umma_desc_sw128(pft_kmajor_step<D>(qa, kk), 16, 1024),
+                    umma_f16(taddr + bf * 128, umma_desc_sw128(pft_kmajor_step<D>(qa, kk), 16, 1024),
                              umma_desc_sw128(pft_kmajor_step<D>(ka, kk), 16, 1024), idesc, kk > 0);
+                umma_commit(&sfull[bf]);
+                umma_commit(&kempty[st]);
             }
-            umma_commit(&bar_s);
+            // no MMA is in flight when the TMEM is released
+            umma_commit(&done);
+            mbar_wait_bounded(&done, 0);
         }
-        __syncwarp();
-        ok = ok && pft_wait(&bar_s, kt & 1, a.err);
-        ok = __all_sync(0xffffffffu, ok);   // TMEM loads are warp-collective
-        tc_fence_after();
-        if (ok) {
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld32(taddr + ((uint32_t)(32 * warp) << 16) + 32 * c, v);
-                tmem_wait_ld();
-                const int kbase = kt * PFT_ROWS + 32 * c;
-                float mx = -INFINITY;
+    } else {
+        const int q4 = warp & 3, hf = warp >> 2;
+        const int r = 32 * q4 + lane;
+        const int qi = q0 + r;
+        const int c0 = 64 * hf;
+        const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+        const float sd = sqrtf((float)D), inv = 1.f / sd;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int kt = 0; kt < nkt; ++kt) {
+            const int bf = kt & 1;
+            ok = ok && pft_wait(&sfull[bf], (kt >> 1) & 1, err);
+            ok = __all_sync(0xffffffffu, ok);     // TMEM loads are warp-collective
+            if (!ok) break;
+            tc_fence_after();
+            float v[64];
+            tmem_ld32(taddr + lane_off + bf * 128 + c0, v);
+            tmem_ld32(taddr + lane_off + bf * 128 + c0 + 32, v + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sempty[bf]);
+            const int kbase = kt * PFT_ROWS + c0;
+            float mx = -INFINITY;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int ki = kbase + i;
-                    v[i] = (ki <= qi && ki < a.S) ? div_r<DT>(rnd<DT>(v[i]), sqrt_d) : -INFINITY;
-                    mx = fmaxf(mx, v[i]);
+            for (int i = 0; i < 64; i += 2) {
+                pft_logit2<DT, D>(v[i], v[i + 1], inv, sd);
+                if (kt == qt) {
+                    if (kbase + i > qi) v[i] = -INFINITY;
+                    if (kbase + i + 1 > qi) v[i + 1] = -INFINITY;
                 }
-                const float mn = fmaxf(m, mx);
-                if (mn > -INFINITY) {
-                    float ps = 0.f;
+                mx = fmaxf(mx, fmaxf(v[i], v[i + 1]));
+            }
+            const float mn = fmaxf(m, mx);
+            if (mn > -INFINITY) {
+                float ps = 0.f;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ps += v[i] > -INFINITY ? expf(v[i] - mn) : 0.f;
-                    l = (m > -INFINITY ? l * expf(m - mn) : 0.f) + ps;
-                    m = mn;
-                }
+                for (int i = 0; i < 64; ++i) ps += pft_ex2((v[i] - mn) * PFT_LOG2E);
+                l = l * pft_ex2((m - mn) * PFT_LOG2E) + ps;
+                m = mn;
             }
         }
-        tc_fence_before();
-        __syncthreads();
+        // the two column halves of a row combine
+        if (hf == 1) { red[r][0] = m; red[r][1] = l; }
+        pft_named_sync(1, 32 * PFT_CW);
+        if (hf == 0 && qi < a.S) {
+            const float m1 = red[r][0], l1 = red[r][1];
+            const float mm = fmaxf(m, m1);
+            const float ll = l * pft_ex2((m - mm) * PFT_LOG2E) + l1 * pft_ex2((m1 - mm) * PFT_LOG2E);
+            float* sp = a.stats + ((((size_t)b * a.H + h) * a.S + qi) * a.G + (hq - h * a.G)) * 2;
+            sp[0] = mm;
+            sp[1] = ll > 0.f ? 1.f / ll : 0.f;
+        }
     }
-    if (qi < a.S) {
-        float* sp = a.stats + (((size_t)b * a.Hq + hq) * a.S + qi) * 2;
-        sp[0] = m;
-        sp[1] = l;
-    }
+    tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, 128);
+    if (warp == PFT_MMA_WARP) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(taddr, 256);
+    }
 }
 
-// ---------------------------------------------------------------- output
-template <int DT, int D>
-__global__ void __launch_bounds__(128, 1) pft_out_kernel(const __grid_constant__ CUtensorMap mQ,
-                                                         const __grid_constant__ CUtensorMap mK,
-                                                         const __grid_constant__ CUtensorMap mV, PftArgs a) {
+// ---------------------------------------------------------------- output + column-sum partials
+// Row tile: QB = 128 / G queries x the G heads of KV head h (row r is query
+// q0 + r / G, head h*G + r % G), so one CTA holds every head of a query and
+// forms the scorer's group mean from the same rounded probabilities that feed
+// P.V.  Per key tile: S = Q.K^T into TMEM (double-buffered); P = exp(l - max)
+// / sum rounded to the KV dtype, written swizzled to shared memory; then two
+// MMAs read P: O += P.V (V MN-major) and, for the column sums, the group sums
+// Gs[key][query] = P^T.W with W[row][query] = 1 when the row belongs to the
+// query (P^T as an MN-major operand).  The compute warps turn Gs into the
+// rounded group means, sum them over the block's queries and store one partial
+// per (query block, key); pft_chunk_kernel folds those into the 512-query
+// chunk sums.
+template <int DT, int D, int G, bool CS>
+__global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_constant__ CUtensorMap mQg,
+                                                                  const __grid_constant__ CUtensorMap mK,
+                                                                  const __grid_constant__ CUtensorMap mV, PftArgs a) {
     using T = typename Elt<DT>::T;
     constexpr int NS = D / 64;
+    constexpr int QB = PFT_ROWS / G;                 // queries per block
+    constexpr int WSLAB = QB * 128;                  // one 64-element slab of W (QB rows)
+    constexpr int HCOL = QB / 2;                     // Gs columns per compute warp
     extern __shared__ unsigned char pft_raw[];
     unsigned char* sm = pft_raw + ((1024u - (smem_u32(pft_raw) & 1023u)) & 1023u);
-    unsigned char* sQ = sm;                              // [NS]
-    unsigned char* sK = sQ + NS * PFT_SLAB;              // [2][NS]
-    unsigned char* sV = sK + 2 * NS * PFT_SLAB;          // [2][NS]
-    unsigned char* sP = sV + 2 * NS * PFT_SLAB;          // [2] slabs: 128 queries x 128 keys
-    __shared__ __align__(8) uint64_t bar_k[2], bar_s, bar_pv;
+    unsigned char* sQ = sm;                          // [NS]
+    unsigned char* sK = sQ + NS * PFT_SLAB;          // [2][NS]
+    unsigned char* sV = sK + 2 * NS * PFT_SLAB;      // [2][NS]
+    unsigned char* sP = sV + 2 * NS * PFT_SLAB;      // 2 slabs: 128 rows x 128 keys
+    unsigned char* sW = sP + 2 * PFT_SLAB;           // 2 slabs of QB rows (column sums only)
+    __shared__ __align__(8) uint64_t bar_q, kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], sempty[2];
+    __shared__ __align__(8) uint64_t pfull, pempty, ofull, done;
+    __shared__ float red[2][PFT_ROWS];
     __shared__ uint32_t s_taddr;
-    const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
-    const int h = hq / a.G;
-    const int warp = threadIdx.x >> 5;
-    const int q0 = qt * PFT_ROWS;
-    const int nkt = qt + 1;
-    const float sqrt_d = sqrtf((float)D);
+    const int qb = gridDim.x - 1 - blockIdx.x;       // longest rows first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = qb * QB;
+    const int qend = min(q0 + QB, a.S);              // the block's queries: [q0, qend)
+    const int nkt = (qend - 1) / PFT_ROWS + 1;       // only the last key tile crosses the diagonal
+    int* err = a.err;
 
-    if (warp == 0) { tmem_alloc(&s_taddr, 256); tmem_relinquish(); }
+    if (warp == PFT_MMA_WARP) { tmem_alloc(&s_taddr, 512); tmem_relinquish(); }
     if (threadIdx.x == 0) {
-        mbar_init(&bar_k[0], 1); mbar_init(&bar_k[1], 1); mbar_init(&bar_s, 1); mbar_init(&bar_pv, 1);
+        mbar_init(&bar_q, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1);
+            mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1);
+            mbar_init(&sfull[s], 1); mbar_init(&sempty[s], PFT_CW);
+        }
+        mbar_init(&pfull, PFT_CW); mbar_init(&pempty, 1); mbar_init(&ofull, 1); mbar_init(&done, 1);
         fence_barrier_init();
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t taddr = s_taddr;            // S: columns [0, 128); O: [128, 128 + D)
-    const uint32_t id_s = umma_idesc_f16(DT == QV_BF16, 128, 128, 0, 0);
-    const uint32_t id_o = umma_idesc_f16(DT == QV_BF16, 128, D, 0, 1);
-    if (threadIdx.x == 0) {
-        prefetch_tensormap(&mQ);
-        prefetch_tensormap(&mK);
-        prefetch_tensormap(&mV);
-        mbar_arrive_expect_tx(&bar_k[0], 3 * NS * PFT_SLAB);
-        for (int s = 0; s < NS; ++s) {
-            tma_load_4d(sQ + s * PFT_SLAB, &mQ, 64 * s, hq, q0, b, &bar_k[0]);
-            tma_load_4d(sK + s * PFT_SLAB, &mK, 64 * s, h, 0, b, &bar_k[0]);
-            tma_load_4d(sV + s * PFT_SLAB, &mV, 64 * s, h, 0, b, &bar_k[0]);
-        }
-    }
-    const int r = threadIdx.x;
-    const int qi = q0 + r;
-    float m = 0.f, linv = 0.f;
-    if (qi < a.S) {
-        const float* sp = a.stats + (((size_t)b * a.Hq + hq) * a.S + qi) * 2;
-        m = sp[0];
-        linv = sp[1] > 0.f ? 1.f / sp[1] : 0.f;
-    }
-    bool ok = true;
-    for (int kt = 0; kt < nkt; ++kt) {
-        const int st = kt & 1;
-        // the previous tile's P.V has read P and its K/V stage
-        if (kt > 0) ok = ok && pft_wait(&bar_pv, (kt - 1) & 1, a.err);
-        if (threadIdx.x == 0) {
-            if (kt + 1 < nkt) {
-                mbar_arrive_expect_tx(&bar_k[st ^ 1], 2 * NS * PFT_SLAB);
-                for (int s = 0; s < NS; ++s) {
-                    tma_load_4d(sK + ((st ^ 1) * NS + s) * PFT_SLAB, &mK, 64 * s, h, (kt + 1) * PFT_ROWS, b, &bar_k[st ^ 1]);
-                    tma_load_4d(sV + ((st ^ 1) * NS + s) * PFT_SLAB, &mV, 64 * s, h, (kt + 1) * PFT_ROWS, b, &bar_k[st ^ 1]);
-                }
-            }
-            if (pft_wait(&bar_k[st], (kt >> 1) & 1, a.err)) {
-                tc_fence_after();
-                const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + st * NS * PFT_SLAB);
+    if (CS) {
+        // W, K-major (K = the 128 rows), 128-byte swizzle: stored 16-byte chunk sc
+        // of row n holds the row's logical chunk sc ^ (n & 7)
+        const uint32_t one = DT == QV_BF16 ? 0x3F80u : 0x3C00u;
+        for (int i = threadIdx.x; i < 2 * WSLAB / 16; i += PFT_THREADS) {
+            const int s = i / (WSLAB / 16), rem = i % (WSLAB / 16), n = rem >> 3, sc = rem & 7;
+            const int kb = s * 64 + ((sc ^ (n & 7)) << 3);
+            uint32_t w[4];
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(taddr, umma_desc_sw128(pft_kmajor_step<D>(qa, kk), 16, 1024),
-                             umma_desc_sw128(pft_kmajor_step<D>(ka, kk), 16, 1024), id_s, kk > 0);
-            }
-            umma_commit(&bar_s);
-        }
-        __syncwarp();
-        ok = ok && pft_wait(&bar_s, kt & 1, a.err);
-        ok = __all_sync(0xffffffffu, ok);   // TMEM loads are warp-collective
-        tc_fence_after();
-        // P row r: 128 keys as 16 chunks of 8, written with the 128-byte swizzle
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-            float v[32];
-            if (ok) {
-                tmem_ld32(taddr + ((uint32_t)(32 * warp) << 16) + 32 * c, v);
-                tmem_wait_ld();
-            }
-            const int kbase = kt * PFT_ROWS + 32 * c;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e2 = 0; e2 < 4; ++e2) {
-                    float p2[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int i = 8 * j + 2 * e2 + u;
-                        const int ki = kbase + i;
-                        p2[u] = (ok && ki <= qi && ki < a.S && qi < a.S)
-                                    ? expf(div_r<DT>(rnd<DT>(v[i]), sqrt_d) - m) * linv : 0.f;
-                    }
-                    if (DT == QV_BF16) {
-                        const __nv_bfloat162 x = __floats2bfloat162_rn(p2[0], p2[1]);
-                        w[e2] = *reinterpret_cast<const uint32_t*>(&x);
-                    } else {
-                        const __half2 x = __floats2half2_rn(p2[0], p2[1]);
-                        w[e2] = *reinterpret_cast<const uint32_t*>(&x);
-                    }
-                }
-                const int col8 = 4 * c + j;                 // 8-key chunk index 0..15
-                const int slab = col8 >> 3, ch = col8 & 7;
-                *reinterpret_cast<uint4*>(sP + slab * PFT_SLAB + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-            }
+            for (int e = 0; e < 4; ++e)
+                w[e] = ((kb + 2 * e) / G == n ? one : 0u) | ((kb + 2 * e + 1) / G == n ? one << 16 : 0u);
+            *reinterpret_cast<uint4*>(sW + s * WSLAB + n * 128 + sc * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            tc_fence_after();
-            const uint32_t pa = smem_u32(sP), va = smem_u32(sV + st * NS * PFT_SLAB);
-#pragma unroll
-            for (int kk = 0; kk < PFT_ROWS / 16; ++kk)
-                umma_f16(taddr + 128, umma_desc_sw128(pft_kmajor_step<128>(pa, kk), 16, 1024),
-                         umma_desc_sw128(va + kk * 2048, PFT_SLAB, 1024), id_o, (kt > 0 || kk > 0) ? 1 : 0);
-            umma_commit(&bar_pv);
-        }
-        __syncwarp();
     }
-    ok = ok && pft_wait(&bar_pv, (nkt - 1) & 1, a.err);
-    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_before();
+    __syncthreads();
     tc_fence_after();
-    if (ok) {
-        // every lane of the warp takes part in the (warp-collective) TMEM loads;
-        // only rows inside the sequence are stored
-        T* orow = reinterpret_cast<T*>(a.out) + (((size_t)b * a.S + qi) * a.Hq + hq) * D;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-            float v[32];
-            tmem_ld32(taddr + ((uint32_t)(32 * warp) << 16) + 128 + 32 * c, v);
-            tmem_wait_ld();
-            if (qi < a.S) {
+    const uint32_t taddr = s_taddr;   // S: [0, 256) as two buffers; O: [256, 256 + D); Gs: [384, 384 + QB)
+
+    if (warp == PFT_TMA_WARP) {
+        if (lane == 0) {
+            prefetch_tensormap(&mQg);
+            prefetch_tensormap(&mK);
+            prefetch_tensormap(&mV);
+            mbar_arrive_expect_tx(&bar_q, NS * PFT_SLAB);
+            for (int s = 0; s < NS; ++s) tma_load_4d(sQ + s * PFT_SLAB, &mQg, 64 * s, h * G, q0, b, &bar_q);
+            int ik = 0, iv = 0;
+            bool ok = true;
+            for (int kt = 0; kt < nkt; ++kt) {
+                const int st = kt & 1;
+                if (kt >= 2) ok = ok && pft_wait(&kempty[st], ((kt >> 1) - 1) & 1, err);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&kfull[st], NS * PFT_SLAB);
+                for (int s = 0; s < NS; ++s)
+                    tma_load_4d(sK + (st * NS + s) * PFT_SLAB, &mK, 64 * s, h, kt * PFT_ROWS, b, &kfull[st]);
+                ik = kt + 1;
+                if (kt >= 2) ok = ok && pft_wait(&vempty[st], ((kt >> 1) - 1) & 1, err);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&vfull[st], NS * PFT_SLAB);
+                for (int s = 0; s < NS; ++s)
+                    tma_load_4d(sV + (st * NS + s) * PFT_SLAB, &mV, 64 * s, h, kt * PFT_ROWS, b, &vfull[st]);
+                iv = kt + 1;
+            }
+            // the copies this thread issued have landed before the CTA exits
+            mbar_wait_bounded(&bar_q, 0);
+            for (int kt = ik - 2 > 0 ? ik - 2 : 0; kt < ik; ++kt) mbar_wait_bounded(&kfull[kt & 1], (kt >> 1) & 1);
+            for (int kt = iv - 2 > 0 ? iv - 2 : 0; kt < iv; ++kt) mbar_wait_bounded(&vfull[kt & 1], (kt >> 1) & 1);
+        }
+    } else if (warp == PFT_MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t id_s = umma_idesc_f16(DT == QV_BF16, 128, 128, 0, 0);
+            const uint32_t id_o = umma_idesc_f16(DT == QV_BF16, 128, D, 0, 1);
+            const uint32_t id_g = umma_idesc_f16(DT == QV_BF16, 128, QB, 1, 0);
+            bool ok = pft_wait(&bar_q, 0, err);
+            for (int kt = 0; kt <= nkt && ok; ++kt) {
+                if (kt < nkt) {                  // S(kt) = Q.K(kt)^T
+                    const int st = kt & 1;
+                    ok = pft_wait(&kfull[st], (kt >> 1) & 1, err);
+                    if (ok && kt >= 2) ok = pft_wait(&sempty[st], ((kt >> 1) - 1) & 1, err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK + st * NS * PFT_SLAB);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) orow[32 * c + i] = Elt<DT>::t(v[i]);
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        umma_f16(taddr + st * 128, umma_desc_sw128(pft_kmajor_step<D>(qa, kk), 16, 1024),
+                                 umma_desc_sw128(pft_kmajor_step<D>(ka, kk), 16, 1024), id_s, kk > 0);
+                    umma_commit(&sfull[st]);
+                    umma_commit(&kempty[st]);
+                }
+                if (kt >= 1) {                   // tile j = kt - 1: O += P.V, Gs = P^T.W
+                    const int j = kt - 1, st = j & 1;
+                    ok = pft_wait(&pfull, j & 1, err);
+                    if (ok) ok = pft_wait(&vfull[st], (j >> 1) & 1, err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t pa = smem_u32(sP), va = smem_u32(sV + st * NS * PFT_SLAB);
+#pragma unroll
+                    for (int kk = 0; kk < PFT_ROWS / 16; ++kk)
+                        umma_f16(taddr + 256, umma_desc_sw128(pft_kmajor_step<128>(pa, kk), 16, 1024),
+                                 umma_desc_sw128(va + kk * 2048, PFT_SLAB, 1024), id_o, (j > 0 || kk > 0) ? 1 : 0);
+                    if (CS) {
+                        const uint32_t wa = smem_u32(sW);
+#pragma unroll
+                        for (int kk = 0; kk < PFT_ROWS / 16; ++kk)
+                            umma_f16(taddr + 384, umma_desc_sw128(pa + kk * 2048, PFT_SLAB, 1024),
+                                     umma_desc_sw128(wa + (kk >> 2) * WSLAB + (kk & 3) * 32, 16, 1024), id_g,
+                                     kk > 0);
+                    }
+                    umma_commit(&pempty);
+                    umma_commit(&vempty[st]);
+                }
+            }
+            if (ok) umma_commit(&ofull);
+            // no MMA is in flight when the TMEM is released
+            umma_commit(&done);
+            mbar_wait_bounded(&done, 0);
+        }
+    } else {
+        const int q4 = warp & 3, hf = warp >> 2;
+        const int r = 32 * q4 + lane;
+        const int qi = q0 + r / G;
+        const int c0 = 64 * hf;
+        const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+        const float sd = sqrtf((float)D), inv = 1.f / sd;
+        float m = 0.f, linv = 0.f;                   // outside the sequence: p = 0
+        if (qi < a.S) {
+            const float* sp = a.stats + ((((size_t)b * a.H + h) * a.S + qi) * G + r % G) * 2;
+            m = sp[0];
+            linv = sp[1];
+        }
+        float* part_row = nullptr;                   // this block's row of column-sum partials
+        if (CS) {
+            const int n = (a.S + QB - 1) / QB;
+            const size_t per_head = (size_t)QB * n * (n + 1) / 2;
+            part_row = a.partial + ((size_t)b * a.H + h) * per_head + (size_t)QB * qb * (qb + 1) / 2;
+        }
+        // column-sum partials of key tile t from Gs (every compute warp calls this
+        // once per tile, failed or not, so the named barrier always pairs up)
+        auto cs_tile = [&](bool okk, int t) {
+            float part = 0.f;
+            if (okk) {
+                tc_fence_after();
+                float gv[HCOL];
+                const uint32_t ga = taddr + lane_off + 384 + hf * HCOL;
+                if constexpr (HCOL == 64) { tmem_ld32(ga, gv); tmem_ld32(ga + 32, gv + 32); }
+                else if constexpr (HCOL == 32) tmem_ld32(ga, gv);
+                else if constexpr (HCOL == 16) tmem_ld16(ga, gv);
+                else tmem_ld8(ga, gv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < HCOL; ++c) part += rnd<DT>(gv[c] * (1.f / G));
+            }
+            tc_fence_before();
+            if (hf == 1) red[t & 1][r] = part;
+            pft_named_sync(1, 32 * PFT_CW);
+            const int key = t * PFT_ROWS + r;
+            if (hf == 0 && okk && key < qend) part_row[key] = part + red[t & 1][r];
+        };
+        bool ok = true;
+        for (int kt = 0; kt < nkt; ++kt) {
+            const int bf = kt & 1;
+            uint32_t w[32];
+            if (ok) ok = pft_wait(&sfull[bf], (kt >> 1) & 1, err);
+            ok = __all_sync(0xffffffffu, ok);       // TMEM loads are warp-collective
+            if (ok) {
+                tc_fence_after();
+                float v[64];
+                tmem_ld32(taddr + lane_off + bf * 128 + c0, v);
+                tmem_ld32(taddr + lane_off + bf * 128 + c0 + 32, v + 32);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sempty[bf]);
+                const int kbase = kt * PFT_ROWS + c0;
+                const bool diag = kt == nkt - 1;
+#pragma unroll
+                for (int i = 0; i < 64; i += 2) {
+                    pft_logit2<DT, D>(v[i], v[i + 1], inv, sd);
+                    float p0 = pft_ex2((v[i] - m) * PFT_LOG2E) * linv;
+                    float p1 = pft_ex2((v[i + 1] - m) * PFT_LOG2E) * linv;
+                    if (diag) {
+                        if (kbase + i > qi) p0 = 0.f;
+                        if (kbase + i + 1 > qi) p1 = 0.f;
+                    }
+                    w[i >> 1] = pft_pack<DT>(p1, p0);
+                }
+            }
+            if (kt >= 1) {
+                // P(kt-1) has been read by its MMAs before P(kt) overwrites it
+                if (ok) ok = pft_wait(&pempty, (kt - 1) & 1, err);
+                ok = __all_sync(0xffffffffu, ok);
+                if (CS) cs_tile(ok, kt - 1);
+            }
+            if (ok) {
+                // row r of slab hf: 8 chunks of 16 bytes, 128-byte swizzle
+                unsigned char* prow = sP + hf * PFT_SLAB + r * 128;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch)
+                    *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+                        make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pfull);
+            }
+        }
+        if (ok) ok = pft_wait(&ofull, 0, err);
+        ok = __all_sync(0xffffffffu, ok);
+        if (CS) cs_tile(ok, nkt - 1);
+        if (ok) {
+            tc_fence_after();
+            constexpr int HC = D / 2;                    // this thread's output columns
+            T* orow = reinterpret_cast<T*>(a.out) + (((size_t)b * a.S + qi) * a.Hq + h * G + r % G) * D + hf * HC;
+#pragma unroll
+            for (int c = 0; c < HC; c += 32) {
+                float v[32];
+                tmem_ld32(taddr + lane_off + 256 + hf * HC + c, v);
+                tmem_wait_ld();
+                if (qi < a.S) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 u;
+                        u.x = pft_pack<DT>(v[i + 1], v[i]);
+                        u.y = pft_pack<DT>(v[i + 3], v[i + 2]);
+                        u.z = pft_pack<DT>(v[i + 5], v[i + 4]);
+                        u.w = pft_pack<DT>(v[i + 7], v[i + 6]);
+                        *reinterpret_cast<uint4*>(orow + c + i) = u;
+                    }
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, 256);
+    if (warp == PFT_MMA_WARP) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(taddr, 512);
+    }
 }
 
-// ---------------------------------------------------------------- column sums
-template <int DT, int D>
-__global__ void __launch_bounds__(128, 1) pft_colsum_kernel(const __grid_constant__ CUtensorMap mK,
-                                                            const __grid_constant__ CUtensorMap mQg, PftArgs a) {
-    constexpr int NS = D / 64;
-    extern __shared__ unsigned char pft_raw[];
-    unsigned char* sm = pft_raw + ((1024u - (smem_u32(pft_raw) & 1023u)) & 1023u);
-    const int G = a.G;
-    const int N = PFT_QB * G;                            // (query, head) columns per step
-    const int qslab = N * 128;                           // bytes of one slab of a query block
-    unsigned char* sK = sm;                              // [NS]
-    unsigned char* sQ = sK + NS * PFT_SLAB;              // [2][NS] slabs of N rows
-    float* s_st = reinterpret_cast<float*>(sQ + 2 * NS * qslab);   // [2][N][2]
-    __shared__ __align__(8) uint64_t bar_q[2], bar_s;
-    __shared__ uint32_t s_taddr;
-    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int warp = threadIdx.x >> 5;
-    const int k0 = kt * PFT_ROWS;
-    const int key = k0 + threadIdx.x;
-    const int qb0 = k0 / PFT_QB;
-    const int nqb = (a.S + PFT_QB - 1) / PFT_QB - qb0;
-    const float sqrt_d = sqrtf((float)D);
-
-    if (warp == 0) { tmem_alloc(&s_taddr, 256); tmem_relinquish(); }
-    if (threadIdx.x == 0) {
-        mbar_init(&bar_q[0], 1); mbar_init(&bar_q[1], 1); mbar_init(&bar_s, 1);
-        fence_barrier_init();
+// Column sums from the partials: per key, the blocks of each 512-query chunk
+// summed in order and rounded to the KV dtype, chunks accumulated in fp32
+// (blocks that end before the key hold nothing for it and are not read).
+template <int DT>
+__global__ void pft_chunk_kernel(const float* __restrict__ partial, float* __restrict__ colsum, int S, int H,
+                                 int QB) {
+    const int key = blockIdx.x * blockDim.x + threadIdx.x;
+    const int h = blockIdx.y, b = blockIdx.z;
+    if (key >= S) return;
+    const int n = (S + QB - 1) / QB;
+    const float* base = partial + ((size_t)b * H + h) * ((size_t)QB * n * (n + 1) / 2);
+    const int bpc = PFT_CHUNK / QB;
+    int j = key / QB;
+    float acc = 0.f;
+    while (j < n) {
+        const int cend = min((j / bpc + 1) * bpc, n);
+        float s = 0.f;
+        for (; j < cend; ++j) s += base[(size_t)QB * j * (j + 1) / 2 + key];
+        acc += rnd<DT>(s);
     }
-    auto load_stats = [&](int j, int buf) {
-        for (int t = threadIdx.x; t < N; t += blockDim.x) {
-            const int qi = (qb0 + j) * PFT_QB + t / G, hq = h * G + t % G;
-            float mv = 0.f, lv = 1.f;
-            if (qi < a.S) {
-                const float* sp = a.stats + (((size_t)b * a.Hq + hq) * a.S + qi) * 2;
-                mv = sp[0];
-                lv = sp[1];
-            }
-            s_st[(buf * N + t) * 2] = mv;
-            s_st[(buf * N + t) * 2 + 1] = lv;
-        }
-    };
-    load_stats(0, 0);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t taddr = s_taddr;
-    const uint32_t idesc = umma_idesc_f16(DT == QV_BF16, 128, N, 0, 0);
-    if (threadIdx.x == 0) {
-        prefetch_tensormap(&mK);
-        prefetch_tensormap(&mQg);
-        mbar_arrive_expect_tx(&bar_q[0], NS * PFT_SLAB + NS * qslab);
-        for (int s = 0; s < NS; ++s) {
-            tma_load_4d(sK + s * PFT_SLAB, &mK, 64 * s, h, k0, b, &bar_q[0]);
-            tma_load_4d(sQ + s * qslab, &mQg, 64 * s, h * G, qb0 * PFT_QB, b, &bar_q[0]);
-        }
-    }
-    float acc = 0.f, chunk = 0.f;
-    int cur = (qb0 * PFT_QB) / PFT_CHUNK;
-    bool ok = true;
-    for (int j = 0; j < nqb; ++j) {
-        const int st = j & 1;
-        if (threadIdx.x == 0) {
-            if (j + 1 < nqb) {
-                mbar_arrive_expect_tx(&bar_q[st ^ 1], NS * qslab);
-                for (int s = 0; s < NS; ++s)
-                    tma_load_4d(sQ + ((st ^ 1) * NS + s) * qslab, &mQg, 64 * s, h * G, (qb0 + j + 1) * PFT_QB, b,
-                                &bar_q[st ^ 1]);
-            }
-            if (pft_wait(&bar_q[st], (j >> 1) & 1, a.err)) {
-                tc_fence_after();
-                const uint32_t ka = smem_u32(sK), qa = smem_u32(sQ + st * NS * qslab);
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    umma_f16(taddr, umma_desc_sw128(pft_kmajor_step<D>(ka, kk), 16, 1024),
-                             umma_desc_sw128(qa + (uint32_t)((kk >> 2) * qslab + (kk & 3) * 32), 16, 1024), idesc,
-                             kk > 0);
-            }
-            umma_commit(&bar_s);
-        }
-        if (j + 1 < nqb) load_stats(j + 1, st ^ 1);
-        __syncwarp();
-        ok = ok && pft_wait(&bar_s, j & 1, a.err);
-        ok = __all_sync(0xffffffffu, ok);
-        tc_fence_after();
-        const float* stt = s_st + st * N * 2;
-        for (int c0 = 0; c0 < N; c0 += 32) {
-            float v[32];
-            if (ok) {
-                tmem_ld32(taddr + ((uint32_t)(32 * warp) << 16) + c0, v);
-                tmem_wait_ld();
-            }
-            // G consecutive columns are one query's heads (G divides 32)
-            for (int c = 0; c < 32; c += G) {
-                const int qi = (qb0 + j) * PFT_QB + (c0 + c) / G;
-                if (qi >= a.S) break;
-                const int ch = qi / PFT_CHUNK;
-                if (ch != cur) {
-                    acc += rnd<DT>(chunk);
-                    chunk = 0.f;
-                    cur = ch;
-                }
-                if (!ok || key > qi || key >= a.S) continue;
-                float ps = 0.f;
-                for (int gi = 0; gi < G; ++gi) {
-                    const int n = c0 + c + gi;
-                    const float lg = div_r<DT>(rnd<DT>(v[c + gi]), sqrt_d);
-                    ps += rnd<DT>(expf(lg - stt[2 * n]) / stt[2 * n + 1]);
-                }
-                chunk += rnd<DT>(ps / (float)G);
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-    }
-    acc += rnd<DT>(chunk);
-    if (key < a.S) a.colsum[((size_t)b * a.H + h) * a.S + key] = acc;
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, 256);
+    colsum[((size_t)b * H + h) * S + key] = acc;
 }
 
 // ---------------------------------------------------------------- host
@@ -463,43 +603,73 @@ bool pft_supported(const Geo& g) {
            (g.G == 1 || g.G == 2 || g.G == 4 || g.G == 8);
 }
 
+// Bytes of the column-sum partials: per (sequence, KV head) a triangle of
+// n (n + 1) / 2 rows of QB keys, n = ceil(S / QB), QB = 128 / G.
+size_t pft_partial_bytes(const Geo& g, int S) {
+    const size_t QB = PFT_ROWS / g.G, n = (S + QB - 1) / QB;
+    return (size_t)g.B * g.H * (QB * n * (n + 1) / 2) * sizeof(float);
+}
+
+template <int DT, int D, int G, bool CS>
+static cudaError_t pft_attn_launch(const CUtensorMap& mQg, const CUtensorMap& mK, const CUtensorMap& mV,
+                                   const PftArgs& a, cudaStream_t s) {
+    constexpr int NS = D / 64;
+    const size_t bytes = 1024 + 5 * NS * (size_t)PFT_SLAB + 2 * PFT_SLAB + (CS ? 2 * (PFT_ROWS / G) * 128 : 0);
+    static int c = 48 * 1024;
+    cudaError_t e = ensure_smem(pft_attn_kernel<DT, D, G, CS>, bytes, &c);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((a.S + PFT_ROWS / G - 1) / (PFT_ROWS / G), a.H, a.B);
+    pft_attn_kernel<DT, D, G, CS><<<grid, PFT_THREADS, bytes, s>>>(mQg, mK, mV, a);
+    return cudaSuccess;
+}
+
+template <int DT, int D, int G>
+static cudaError_t pft_attn_g(const CUtensorMap& mQg, const CUtensorMap& mK, const CUtensorMap& mV,
+                              const PftArgs& a, float* colsum, cudaStream_t s) {
+    if (!colsum) return pft_attn_launch<DT, D, G, false>(mQg, mK, mV, a, s);
+    cudaError_t e = pft_attn_launch<DT, D, G, true>(mQg, mK, mV, a, s);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((a.S + 255) / 256, a.H, a.B);
+    pft_chunk_kernel<DT><<<grid, 256, 0, s>>>(a.partial, colsum, a.S, a.H, PFT_ROWS / G);
+    return cudaSuccess;
+}
+
 template <int DT, int D>
 static int pft_launch_t(const Geo& g, const void* q, const void* k, const void* v, int S, void* out, float* colsum,
-                        float* stats, int* err, cudaStream_t s) {
+                        float* stats, float* partial, int* err, cudaStream_t s) {
     const int Hq = g.H * g.G;
     CUtensorMap mQ, mK, mV, mQg;
     if (!pft_map(&mQ, q, DT, D, Hq, S, g.B, 1, PFT_ROWS) || !pft_map(&mK, k, DT, D, g.H, S, g.B, 1, PFT_ROWS) ||
-        !pft_map(&mV, v, DT, D, g.H, S, g.B, 1, PFT_ROWS) || !pft_map(&mQg, q, DT, D, Hq, S, g.B, g.G, PFT_QB))
+        !pft_map(&mV, v, DT, D, g.H, S, g.B, 1, PFT_ROWS) ||
+        !pft_map(&mQg, q, DT, D, Hq, S, g.B, g.G, PFT_ROWS / g.G))
         return QV_EINVAL;
     PftArgs a;
     a.S = S; a.B = g.B; a.H = g.H; a.G = g.G; a.Hq = Hq;
-    a.stats = stats; a.out = out; a.colsum = colsum; a.err = err;
+    a.stats = stats; a.out = out; a.partial = partial; a.err = err;
     constexpr int NS = D / 64;
-    const size_t sm_stats = 1024 + 3 * NS * PFT_SLAB;
-    const size_t sm_out = 1024 + 5 * NS * PFT_SLAB + 2 * PFT_SLAB;
-    const size_t sm_col = 1024 + NS * PFT_SLAB + 2 * NS * (size_t)PFT_QB * g.G * 128 + 2 * PFT_QB * g.G * 2 * 4;
-    static int c1 = 48 * 1024, c2 = 48 * 1024, c3 = 48 * 1024;
+    const size_t sm_stats = 1024 + 4 * NS * PFT_SLAB;
+    static int c1 = 48 * 1024;
     cudaError_t e = ensure_smem(pft_stats_kernel<DT, D>, sm_stats, &c1);
-    if (e == cudaSuccess) e = ensure_smem(pft_out_kernel<DT, D>, sm_out, &c2);
-    if (e == cudaSuccess) e = ensure_smem(pft_colsum_kernel<DT, D>, sm_col, &c3);
     if (e != cudaSuccess) return set_cuda_error(e);
     const dim3 gq((S + PFT_ROWS - 1) / PFT_ROWS, Hq, g.B);
-    pft_stats_kernel<DT, D><<<gq, 128, sm_stats, s>>>(mQ, mK, a);
-    pft_out_kernel<DT, D><<<gq, 128, sm_out, s>>>(mQ, mK, mV, a);
-    if (colsum) {
-        const dim3 gk((S + PFT_ROWS - 1) / PFT_ROWS, g.H, g.B);
-        pft_colsum_kernel<DT, D><<<gk, 128, sm_col, s>>>(mK, mQg, a);
+    pft_stats_kernel<DT, D><<<gq, PFT_THREADS, sm_stats, s>>>(mQ, mK, a);
+    switch (g.G) {
+        case 1: e = pft_attn_g<DT, D, 1>(mQg, mK, mV, a, colsum, s); break;
+        case 2: e = pft_attn_g<DT, D, 2>(mQg, mK, mV, a, colsum, s); break;
+        case 4: e = pft_attn_g<DT, D, 4>(mQg, mK, mV, a, colsum, s); break;
+        default: e = pft_attn_g<DT, D, 8>(mQg, mK, mV, a, colsum, s); break;
     }
+    if (e != cudaSuccess) return set_cuda_error(e);
     return check_launch();
 }
 
 int pft_launch(const Geo& g, const void* q, const void* k, const void* v, int S, void* out, float* colsum,
-               float* stats, int* err, cudaStream_t s) {
+               float* stats, float* partial, int* err, cudaStream_t s) {
     if (g.dt == QV_BF16)
-        return g.D == 128 ? pft_launch_t<QV_BF16, 128>(g, q, k, v, S, out, colsum, stats, err, s)
-                          : pft_launch_t<QV_BF16, 64>(g, q, k, v, S, out, colsum, stats, err, s);
-    return g.D == 128 ? pft_launch_t<QV_F16, 128>(g, q, k, v, S, out, colsum, stats, err, s)
-                      : pft_launch_t<QV_F16, 64>(g, q, k, v, S, out, colsum, stats, err, s);
+        return g.D == 128 ? pft_launch_t<QV_BF16, 128>(g, q, k, v, S, out, colsum, stats, partial, err, s)
+                          : pft_launch_t<QV_BF16, 64>(g, q, k, v, S, out, colsum, stats, partial, err, s);
+    return g.D == 128 ? pft_launch_t<QV_F16, 128>(g, q, k, v, S, out, colsum, stats, partial, err, s)
+                      : pft_launch_t<QV_F16, 64>(g, q, k, v, S, out, colsum, stats, partial, err, s);
 }
 
 }  // namespace qv

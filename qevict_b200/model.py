@@ -74,10 +74,12 @@ def rope_(x, cos, sin, pos0=0):
     return x
 
 
-def prefill_attention(q, k, v, colsum=True):
+def prefill_attention(q, k, v, colsum=True, check=True):
     """Causal prefill attention + per-key column sums (qv_prefill_attention).
 
-    q [B, S, Hq, D], k/v [B, S, H, D] contiguous -> (out [B, S, Hq, D], colsum [B, H, S] fp32)."""
+    q [B, S, Hq, D], k/v [B, S, H, D] contiguous -> (out [B, S, Hq, D], colsum [B, H, S] fp32).
+    With check, the device error word is read back (a stream synchronisation)
+    and a pipelined kernel that gave up waiting raises QevictError."""
     B, S, Hq, D = q.shape
     H = k.shape[2]
     dims = N.QvDims(B, H, Hq // H, D, 64, 0, 64, 0, 0, 1, 8, kv_dtype_code(q.dtype), 0)
@@ -89,6 +91,13 @@ def prefill_attention(q, k, v, colsum=True):
     rc = N.lib().qv_prefill_attention(ctypes.byref(dims), N.ptr(q), N.ptr(k), N.ptr(v), S, N.ptr(out),
                                       N.ptr(cs), N.ptr(ws), wsb, torch.cuda.current_stream(q.device).cuda_stream)
     N.check(rc, "qv_prefill_attention")
+    if check:
+        err = ctypes.c_int32(0)
+        N.check(N.lib().qv_prefill_read_error(N.ptr(ws), wsb, ctypes.byref(err),
+                                              torch.cuda.current_stream(q.device).cuda_stream),
+                "qv_prefill_read_error")
+        if err.value:
+            raise N.QevictError(f"qv_prefill_attention: device error word {err.value:#x} (a bounded wait gave up)")
     return out, cs
 
 
