@@ -56,6 +56,7 @@ constexpr int PFT_CW = 8;            // compute warps
 constexpr int PFT_TMA_WARP = PFT_CW;
 constexpr int PFT_MMA_WARP = PFT_CW + 1;
 constexpr int PFT_THREADS = 32 * (PFT_CW + 2);
+constexpr int PFT_ACW = 8;           // compute warps of pft_attn_kernel (a multiple of 4)
 constexpr float PFT_LOG2E = 1.4426950408889634f;
 
 struct PftArgs {
@@ -96,6 +97,36 @@ __device__ __forceinline__ float pft_ex2(float x) {
     return y;
 }
 
+// Packed fp32x2 arithmetic (sm_100): two lanes of a 64-bit register pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ void pft_named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -120,24 +151,95 @@ template <int DT> __device__ __forceinline__ void pft_unpack(uint32_t p, float& 
     }
 }
 
-// The reference's logit of an fp32 accumulator pair: round(round(x) / sqrt(D)).
-template <int DT, int D> __device__ __forceinline__ void pft_logit2(float& a, float& b, float inv, float sd) {
-    float ra, rb;
-    pft_unpack<DT>(pft_pack<DT>(a, b), ra, rb);
-    float qa = __fmul_rn(ra, inv), qb = __fmul_rn(rb, inv);
-    if (DT == QV_F16 && D != 64) {
-        qa = __fmaf_rn(__fmaf_rn(-qa, sd, ra), inv, qa);
-        qb = __fmaf_rn(__fmaf_rn(-qb, sd, rb), inv, qb);
+// Packed maximum of two KV-dtype pairs, and a packed -inf.
+template <int DT> __device__ __forceinline__ uint32_t pft_max2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    if (DT == QV_BF16)
+        asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    else
+        asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+template <int DT> __device__ __forceinline__ uint32_t pft_ninf() { return DT == QV_BF16 ? 0xFF80u : 0xFC00u; }
+
+// The reference's logits of an fp32 accumulator pair, round(round(x) / sqrt(D)),
+// packed in the KV dtype (x0 in the low half).  inv2 = 1/sqrt(D) twice,
+// nsd2 = -sqrt(D) twice (the fp16, D = 128 residual step).
+template <int DT, int D>
+__device__ __forceinline__ uint32_t pft_logit2(float x0, float x1, uint64_t inv2, uint64_t nsd2) {
+    float r0, r1;
+    pft_unpack<DT>(pft_pack<DT>(x1, x0), r1, r0);
+    const uint64_t r = f2_pack(r0, r1);
+    uint64_t q = f2_mul(r, inv2);
+    if (DT == QV_F16 && D != 64) q = f2_fma(f2_fma(q, nsd2, r), inv2, q);
+    float q0, q1;
+    f2_unpack(q, q0, q1);
+    return pft_pack<DT>(q1, q0);
+}
+
+// One score tile's 64 columns of a row, statistics pass: running max m and
+// sum l of exp(logit - m).  DIAG: keys above the row's query are masked.
+template <int DT, int D, bool DIAG>
+__device__ __forceinline__ void pft_stats_tile(const float* v, int kbase, int qi, uint64_t inv2, uint64_t nsd2,
+                                               float& m, float& l) {
+    uint32_t lg[32];
+    uint32_t mx2 = pft_ninf<DT>() * 0x10001u;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        uint32_t x = pft_logit2<DT, D>(v[2 * j], v[2 * j + 1], inv2, nsd2);
+        if (DIAG) {
+            if (kbase + 2 * j > qi) x = (x & 0xFFFF0000u) | pft_ninf<DT>();
+            if (kbase + 2 * j + 1 > qi) x = (x & 0xFFFFu) | (pft_ninf<DT>() << 16);
+        }
+        lg[j] = x;
+        mx2 = pft_max2<DT>(mx2, x);
     }
-    pft_unpack<DT>(pft_pack<DT>(qa, qb), a, b);
+    float mh, ml;
+    pft_unpack<DT>(mx2, mh, ml);
+    const float mn = fmaxf(m, fmaxf(mh, ml));
+    if (mn > -INFINITY) {
+        const uint64_t mn2 = f2_pack(mn, mn), l2e = f2_pack(PFT_LOG2E, PFT_LOG2E);
+        uint64_t ps2 = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            float a, b, d0, d1;
+            pft_unpack<DT>(lg[j], b, a);
+            f2_unpack(f2_mul(f2_sub(f2_pack(a, b), mn2), l2e), d0, d1);
+            ps2 = f2_add(ps2, f2_pack(pft_ex2(d0), pft_ex2(d1)));
+        }
+        float p0, p1;
+        f2_unpack(ps2, p0, p1);
+        l = l * pft_ex2((m - mn) * PFT_LOG2E) + (p0 + p1);
+        m = mn;
+    }
+}
+
+// NC columns of a row of one score tile, output pass: P = exp(logit - m) / sum
+// rounded to the KV dtype, packed in pairs (w[j] = keys 2j, 2j+1).
+template <int DT, int D, bool DIAG, int NC>
+__device__ __forceinline__ void pft_prob_tile(const float* v, int kbase, int qi, uint64_t inv2, uint64_t nsd2,
+                                              uint64_t m2, uint64_t li2, uint32_t* w) {
+    const uint64_t l2e = f2_pack(PFT_LOG2E, PFT_LOG2E);
+#pragma unroll
+    for (int j = 0; j < NC / 2; ++j) {
+        float a, b, d0, d1, p0, p1;
+        pft_unpack<DT>(pft_logit2<DT, D>(v[2 * j], v[2 * j + 1], inv2, nsd2), b, a);
+        f2_unpack(f2_mul(f2_sub(f2_pack(a, b), m2), l2e), d0, d1);
+        f2_unpack(f2_mul(f2_pack(pft_ex2(d0), pft_ex2(d1)), li2), p0, p1);
+        if (DIAG) {
+            if (kbase + 2 * j > qi) p0 = 0.f;
+            if (kbase + 2 * j + 1 > qi) p1 = 0.f;
+        }
+        w[j] = pft_pack<DT>(p1, p0);
+    }
 }
 
 // ---------------------------------------------------------------- stats
 template <int DT, int D>
-__global__ void __launch_bounds__(PFT_THREADS, 1) pft_stats_kernel(const __grid_constant__ CUtensorMap mQ,
+__global__ void __launch_bounds__(PFT_THREADS, 2) pft_stats_kernel(const __grid_constant__ CUtensorMap mQ,
                                                                    const __grid_constant__ CUtensorMap mK, PftArgs a) {
     constexpr int NS = D / 64;                   // slabs per operand tile
-    constexpr int KST = 3;                       // K stages
+    constexpr int KST = 2;                       // K stages (two CTAs share an SM)
     extern __shared__ unsigned char pft_raw[];
     unsigned char* sm = pft_raw + ((1024u - (smem_u32(pft_raw) & 1023u)) & 1023u);
     unsigned char* sQ = sm;                      // [NS]
@@ -217,6 +319,7 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_stats_kernel(const __grid_
         const int c0 = 64 * hf;
         const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
         const float sd = sqrtf((float)D), inv = 1.f / sd;
+        const uint64_t inv2 = f2_pack(inv, inv), nsd2 = f2_pack(-sd, -sd);
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int kt = 0; kt < nkt; ++kt) {
@@ -233,24 +336,8 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_stats_kernel(const __grid_
             __syncwarp();
             if (lane == 0) mbar_arrive(&sempty[bf]);
             const int kbase = kt * PFT_ROWS + c0;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-                pft_logit2<DT, D>(v[i], v[i + 1], inv, sd);
-                if (kt == qt) {
-                    if (kbase + i > qi) v[i] = -INFINITY;
-                    if (kbase + i + 1 > qi) v[i + 1] = -INFINITY;
-                }
-                mx = fmaxf(mx, fmaxf(v[i], v[i + 1]));
-            }
-            const float mn = fmaxf(m, mx);
-            if (mn > -INFINITY) {
-                float ps = 0.f;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) ps += pft_ex2((v[i] - mn) * PFT_LOG2E);
-                l = l * pft_ex2((m - mn) * PFT_LOG2E) + ps;
-                m = mn;
-            }
+            if (kt == qt) pft_stats_tile<DT, D, true>(v, kbase, qi, inv2, nsd2, m, l);
+            else pft_stats_tile<DT, D, false>(v, kbase, qi, inv2, nsd2, m, l);
         }
         // the two column halves of a row combine
         if (hf == 1) { red[r][0] = m; red[r][1] = l; }
@@ -286,24 +373,32 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_stats_kernel(const __grid_
 // per (query block, key); pft_chunk_kernel folds those into the 512-query
 // chunk sums.
 template <int DT, int D, int G, bool CS>
-__global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_constant__ CUtensorMap mQg,
+__global__ void __launch_bounds__(32 * (PFT_ACW + 2), 1) pft_attn_kernel(const __grid_constant__ CUtensorMap mQg,
                                                                   const __grid_constant__ CUtensorMap mK,
                                                                   const __grid_constant__ CUtensorMap mV, PftArgs a) {
     using T = typename Elt<DT>::T;
     constexpr int NS = D / 64;
     constexpr int QB = PFT_ROWS / G;                 // queries per block
-    constexpr int WSLAB = QB * 128;                  // one 64-element slab of W (QB rows)
-    constexpr int HCOL = QB / 2;                     // Gs columns per compute warp
+    // W: N = QB columns selecting each query's G rows; with G = 1 the block's
+    // partial is the plain column sum of P, one column of ones (N = 16)
+    constexpr int NW = G == 1 ? 16 : QB;
+    constexpr int WSLAB = NW * 128;                  // one 64-element slab of W (NW rows)
+    constexpr int CW = PFT_ACW, NT = 32 * (CW + 2);  // compute warps, threads
+    constexpr int TMA_W = CW, MMA_W = CW + 1;        // the TMA and MMA warps
+    constexpr int NPART = CW / 4;                    // compute warps per TMEM lane quarter
+    constexpr int NC = PFT_ROWS / NPART;             // score columns per compute warp
+    constexpr int HCOL = G == 1 ? 1 : QB / NPART;    // Gs columns per compute warp
+    constexpr int HC = D / NPART;                    // output columns per compute warp
     extern __shared__ unsigned char pft_raw[];
     unsigned char* sm = pft_raw + ((1024u - (smem_u32(pft_raw) & 1023u)) & 1023u);
     unsigned char* sQ = sm;                          // [NS]
     unsigned char* sK = sQ + NS * PFT_SLAB;          // [2][NS]
     unsigned char* sV = sK + 2 * NS * PFT_SLAB;      // [2][NS]
     unsigned char* sP = sV + 2 * NS * PFT_SLAB;      // 2 slabs: 128 rows x 128 keys
-    unsigned char* sW = sP + 2 * PFT_SLAB;           // 2 slabs of QB rows (column sums only)
+    unsigned char* sW = sP + 2 * PFT_SLAB;           // 2 slabs of NW rows (column sums only)
     __shared__ __align__(8) uint64_t bar_q, kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], sempty[2];
     __shared__ __align__(8) uint64_t pfull, pempty, ofull, done;
-    __shared__ float red[2][PFT_ROWS];
+    __shared__ float red[2][NPART - 1][PFT_ROWS];
     __shared__ uint32_t s_taddr;
     const int qb = gridDim.x - 1 - blockIdx.x;       // longest rows first
     const int h = blockIdx.y, b = blockIdx.z;
@@ -313,28 +408,31 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
     const int nkt = (qend - 1) / PFT_ROWS + 1;       // only the last key tile crosses the diagonal
     int* err = a.err;
 
-    if (warp == PFT_MMA_WARP) { tmem_alloc(&s_taddr, 512); tmem_relinquish(); }
+    if (warp == MMA_W) { tmem_alloc(&s_taddr, 512); tmem_relinquish(); }
     if (threadIdx.x == 0) {
         mbar_init(&bar_q, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&kfull[s], 1); mbar_init(&kempty[s], 1);
             mbar_init(&vfull[s], 1); mbar_init(&vempty[s], 1);
-            mbar_init(&sfull[s], 1); mbar_init(&sempty[s], PFT_CW);
+            mbar_init(&sfull[s], 1); mbar_init(&sempty[s], CW);
         }
-        mbar_init(&pfull, PFT_CW); mbar_init(&pempty, 1); mbar_init(&ofull, 1); mbar_init(&done, 1);
+        mbar_init(&pfull, CW); mbar_init(&pempty, 1); mbar_init(&ofull, 1); mbar_init(&done, 1);
         fence_barrier_init();
     }
     if (CS) {
         // W, K-major (K = the 128 rows), 128-byte swizzle: stored 16-byte chunk sc
         // of row n holds the row's logical chunk sc ^ (n & 7)
         const uint32_t one = DT == QV_BF16 ? 0x3F80u : 0x3C00u;
-        for (int i = threadIdx.x; i < 2 * WSLAB / 16; i += PFT_THREADS) {
+        for (int i = threadIdx.x; i < 2 * WSLAB / 16; i += NT) {
             const int s = i / (WSLAB / 16), rem = i % (WSLAB / 16), n = rem >> 3, sc = rem & 7;
             const int kb = s * 64 + ((sc ^ (n & 7)) << 3);
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                w[e] = ((kb + 2 * e) / G == n ? one : 0u) | ((kb + 2 * e + 1) / G == n ? one << 16 : 0u);
+            for (int e = 0; e < 4; ++e) {
+                const bool s0 = G == 1 ? n == 0 : (kb + 2 * e) / G == n;
+                const bool s1 = G == 1 ? n == 0 : (kb + 2 * e + 1) / G == n;
+                w[e] = (s0 ? one : 0u) | (s1 ? one << 16 : 0u);
+            }
             *reinterpret_cast<uint4*>(sW + s * WSLAB + n * 128 + sc * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_async_smem();
@@ -344,7 +442,7 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
     tc_fence_after();
     const uint32_t taddr = s_taddr;   // S: [0, 256) as two buffers; O: [256, 256 + D); Gs: [384, 384 + QB)
 
-    if (warp == PFT_TMA_WARP) {
+    if (warp == TMA_W) {
         if (lane == 0) {
             prefetch_tensormap(&mQg);
             prefetch_tensormap(&mK);
@@ -373,11 +471,11 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
             for (int kt = ik - 2 > 0 ? ik - 2 : 0; kt < ik; ++kt) mbar_wait_bounded(&kfull[kt & 1], (kt >> 1) & 1);
             for (int kt = iv - 2 > 0 ? iv - 2 : 0; kt < iv; ++kt) mbar_wait_bounded(&vfull[kt & 1], (kt >> 1) & 1);
         }
-    } else if (warp == PFT_MMA_WARP) {
+    } else if (warp == MMA_W) {
         if (lane == 0) {
             const uint32_t id_s = umma_idesc_f16(DT == QV_BF16, 128, 128, 0, 0);
             const uint32_t id_o = umma_idesc_f16(DT == QV_BF16, 128, D, 0, 1);
-            const uint32_t id_g = umma_idesc_f16(DT == QV_BF16, 128, QB, 1, 0);
+            const uint32_t id_g = umma_idesc_f16(DT == QV_BF16, 128, NW, 1, 0);
             bool ok = pft_wait(&bar_q, 0, err);
             for (int kt = 0; kt <= nkt && ok; ++kt) {
                 if (kt < nkt) {                  // S(kt) = Q.K(kt)^T
@@ -423,12 +521,13 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
             mbar_wait_bounded(&done, 0);
         }
     } else {
-        const int q4 = warp & 3, hf = warp >> 2;
+        const int q4 = warp & 3, part_id = warp >> 2;
         const int r = 32 * q4 + lane;
         const int qi = q0 + r / G;
-        const int c0 = 64 * hf;
+        const int c0 = NC * part_id;
         const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
         const float sd = sqrtf((float)D), inv = 1.f / sd;
+        const uint64_t inv2 = f2_pack(inv, inv), nsd2 = f2_pack(-sd, -sd);
         float m = 0.f, linv = 0.f;                   // outside the sequence: p = 0
         if (qi < a.S) {
             const float* sp = a.stats + ((((size_t)b * a.H + h) * a.S + qi) * G + r % G) * 2;
@@ -444,53 +543,71 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
         // column-sum partials of key tile t from Gs (every compute warp calls this
         // once per tile, failed or not, so the named barrier always pairs up)
         auto cs_tile = [&](bool okk, int t) {
+            const int key = t * PFT_ROWS + r;
+            if constexpr (G == 1) {
+                // the block's sum of P for this key, one warp per lane quarter
+                if (part_id == 0 && okk) {
+                    tc_fence_after();
+                    float gv[4];
+                    tmem_ld4(taddr + lane_off + 384, gv);
+                    tmem_wait_ld();
+                    if (key < qend) part_row[key] = gv[0];
+                }
+                tc_fence_before();
+                return;
+            }
             float part = 0.f;
             if (okk) {
                 tc_fence_after();
                 float gv[HCOL];
-                const uint32_t ga = taddr + lane_off + 384 + hf * HCOL;
+                const uint32_t ga = taddr + lane_off + 384 + part_id * HCOL;
                 if constexpr (HCOL == 64) { tmem_ld32(ga, gv); tmem_ld32(ga + 32, gv + 32); }
                 else if constexpr (HCOL == 32) tmem_ld32(ga, gv);
                 else if constexpr (HCOL == 16) tmem_ld16(ga, gv);
-                else tmem_ld8(ga, gv);
+                else if constexpr (HCOL == 8) tmem_ld8(ga, gv);
+                else tmem_ld4(ga, gv);
                 tmem_wait_ld();
+                const uint64_t g2 = f2_pack(1.f / G, 1.f / G);
+                uint64_t acc2 = f2_pack(0.f, 0.f);
 #pragma unroll
-                for (int c = 0; c < HCOL; ++c) part += rnd<DT>(gv[c] * (1.f / G));
+                for (int c = 0; c < HCOL; c += 2) {
+                    float a0, a1, r0, r1;
+                    f2_unpack(f2_mul(f2_pack(gv[c], gv[c + 1]), g2), a0, a1);
+                    pft_unpack<DT>(pft_pack<DT>(a1, a0), r1, r0);
+                    acc2 = f2_add(acc2, f2_pack(r0, r1));
+                }
+                float s0, s1;
+                f2_unpack(acc2, s0, s1);
+                part = s0 + s1;
             }
             tc_fence_before();
-            if (hf == 1) red[t & 1][r] = part;
-            pft_named_sync(1, 32 * PFT_CW);
-            const int key = t * PFT_ROWS + r;
-            if (hf == 0 && okk && key < qend) part_row[key] = part + red[t & 1][r];
+            if (part_id > 0) red[t & 1][part_id - 1][r] = part;
+            pft_named_sync(1, 32 * CW);
+            if (part_id == 0 && okk && key < qend) {
+#pragma unroll
+                for (int u = 0; u < NPART - 1; ++u) part += red[t & 1][u][r];
+                part_row[key] = part;
+            }
         };
         bool ok = true;
         for (int kt = 0; kt < nkt; ++kt) {
             const int bf = kt & 1;
-            uint32_t w[32];
+            uint32_t w[NC / 2];
             if (ok) ok = pft_wait(&sfull[bf], (kt >> 1) & 1, err);
             ok = __all_sync(0xffffffffu, ok);       // TMEM loads are warp-collective
             if (ok) {
                 tc_fence_after();
-                float v[64];
+                float v[NC];
                 tmem_ld32(taddr + lane_off + bf * 128 + c0, v);
-                tmem_ld32(taddr + lane_off + bf * 128 + c0 + 32, v + 32);
+                if constexpr (NC == 64) tmem_ld32(taddr + lane_off + bf * 128 + c0 + 32, v + 32);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sempty[bf]);
                 const int kbase = kt * PFT_ROWS + c0;
-                const bool diag = kt == nkt - 1;
-#pragma unroll
-                for (int i = 0; i < 64; i += 2) {
-                    pft_logit2<DT, D>(v[i], v[i + 1], inv, sd);
-                    float p0 = pft_ex2((v[i] - m) * PFT_LOG2E) * linv;
-                    float p1 = pft_ex2((v[i + 1] - m) * PFT_LOG2E) * linv;
-                    if (diag) {
-                        if (kbase + i > qi) p0 = 0.f;
-                        if (kbase + i + 1 > qi) p1 = 0.f;
-                    }
-                    w[i >> 1] = pft_pack<DT>(p1, p0);
-                }
+                const uint64_t m2 = f2_pack(m, m), li2 = f2_pack(linv, linv);
+                if (kt == nkt - 1) pft_prob_tile<DT, D, true, NC>(v, kbase, qi, inv2, nsd2, m2, li2, w);
+                else pft_prob_tile<DT, D, false, NC>(v, kbase, qi, inv2, nsd2, m2, li2, w);
             }
             if (kt >= 1) {
                 // P(kt-1) has been read by its MMAs before P(kt) overwrites it
@@ -499,11 +616,13 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
                 if (CS) cs_tile(ok, kt - 1);
             }
             if (ok) {
-                // row r of slab hf: 8 chunks of 16 bytes, 128-byte swizzle
-                unsigned char* prow = sP + hf * PFT_SLAB + r * 128;
+                // columns c0 .. c0 + NC of row r: 16-byte chunks of its 64-key
+                // slab, 128-byte swizzle
+                unsigned char* prow = sP + (c0 >> 6) * PFT_SLAB + r * 128;
+                const int ch0 = (c0 & 63) >> 3;
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch)
-                    *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) =
+                for (int ch = 0; ch < NC / 8; ++ch)
+                    *reinterpret_cast<uint4*>(prow + (((ch0 + ch) ^ (r & 7)) << 4)) =
                         make_uint4(w[4 * ch], w[4 * ch + 1], w[4 * ch + 2], w[4 * ch + 3]);
                 fence_async_smem();
                 tc_fence_before();
@@ -516,16 +635,17 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
         if (CS) cs_tile(ok, nkt - 1);
         if (ok) {
             tc_fence_after();
-            constexpr int HC = D / 2;                    // this thread's output columns
-            T* orow = reinterpret_cast<T*>(a.out) + (((size_t)b * a.S + qi) * a.Hq + h * G + r % G) * D + hf * HC;
+            constexpr int OC = HC < 32 ? HC : 32;        // columns per TMEM load
+            T* orow = reinterpret_cast<T*>(a.out) + (((size_t)b * a.S + qi) * a.Hq + h * G + r % G) * D + part_id * HC;
 #pragma unroll
-            for (int c = 0; c < HC; c += 32) {
-                float v[32];
-                tmem_ld32(taddr + lane_off + 256 + hf * HC + c, v);
+            for (int c = 0; c < HC; c += OC) {
+                float v[OC];
+                if constexpr (OC == 32) tmem_ld32(taddr + lane_off + 256 + part_id * HC + c, v);
+                else tmem_ld16(taddr + lane_off + 256 + part_id * HC + c, v);
                 tmem_wait_ld();
                 if (qi < a.S) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
+                    for (int i = 0; i < OC; i += 8) {
                         uint4 u;
                         u.x = pft_pack<DT>(v[i + 1], v[i]);
                         u.y = pft_pack<DT>(v[i + 3], v[i + 2]);
@@ -539,7 +659,7 @@ __global__ void __launch_bounds__(PFT_THREADS, 1) pft_attn_kernel(const __grid_c
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == PFT_MMA_WARP) {
+    if (warp == MMA_W) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(taddr, 512);
@@ -614,12 +734,12 @@ template <int DT, int D, int G, bool CS>
 static cudaError_t pft_attn_launch(const CUtensorMap& mQg, const CUtensorMap& mK, const CUtensorMap& mV,
                                    const PftArgs& a, cudaStream_t s) {
     constexpr int NS = D / 64;
-    const size_t bytes = 1024 + 5 * NS * (size_t)PFT_SLAB + 2 * PFT_SLAB + (CS ? 2 * (PFT_ROWS / G) * 128 : 0);
+    const size_t bytes = 1024 + 5 * NS * (size_t)PFT_SLAB + 2 * PFT_SLAB + (CS ? 2 * (G == 1 ? 16 : PFT_ROWS / G) * 128 : 0);
     static int c = 48 * 1024;
     cudaError_t e = ensure_smem(pft_attn_kernel<DT, D, G, CS>, bytes, &c);
     if (e != cudaSuccess) return e;
     const dim3 grid((a.S + PFT_ROWS / G - 1) / (PFT_ROWS / G), a.H, a.B);
-    pft_attn_kernel<DT, D, G, CS><<<grid, PFT_THREADS, bytes, s>>>(mQg, mK, mV, a);
+    pft_attn_kernel<DT, D, G, CS><<<grid, 32 * (PFT_ACW + 2), bytes, s>>>(mQg, mK, mV, a);
     return cudaSuccess;
 }
 
@@ -647,7 +767,7 @@ static int pft_launch_t(const Geo& g, const void* q, const void* k, const void* 
     a.S = S; a.B = g.B; a.H = g.H; a.G = g.G; a.Hq = Hq;
     a.stats = stats; a.out = out; a.partial = partial; a.err = err;
     constexpr int NS = D / 64;
-    const size_t sm_stats = 1024 + 4 * NS * PFT_SLAB;
+    const size_t sm_stats = 1024 + 3 * NS * PFT_SLAB;
     static int c1 = 48 * 1024;
     cudaError_t e = ensure_smem(pft_stats_kernel<DT, D>, sm_stats, &c1);
     if (e != cudaSuccess) return set_cuda_error(e);
