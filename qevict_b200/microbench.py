@@ -53,7 +53,9 @@ def build(batch, sticky, qwin, local, seed=0, dtype=torch.bfloat16):
     return st, g
 
 
-def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=False):
+def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=False, fold=True):
+    """fold=False times the attention without its vote-ledger fold
+    (qv_decode_attention_nofold); the fold then runs after the timed span."""
     st, g = build(batch, sticky, qwin, local)
     q = torch.randn(batch, H * G, D, generator=g, device="cuda").to(st.dtype) * 0.3
     kn = torch.randn(batch, H, D, generator=g, device="cuda").to(st.dtype)
@@ -76,8 +78,10 @@ def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=Fal
         ev[0].record()
         qr = st.append(q, kn, vn)
         ev[1].record()
-        st.attend(qr, out)
+        st.attend(qr, out, fold=fold)
         ev[2].record()
+        if not fold:
+            st.fold()
         t = (st.n_tokens - st.prompt_len - 1) % st.omega + 1
         cyc = st.cycle_due()
         if cyc:
@@ -98,7 +102,7 @@ def run(batch=64, steps=1000, warmup=8, sticky=32, qwin=64, local=512, quiet=Fal
         "avg_bytes_per_launch": sum(by) / len(by),
         "cycle_us_avg": (sum(c for c, t in zip(cyc_t, tvals) if t == OMEGA) / max(1, n_cyc)) * 1e6,
         "cycle_fraction_of_step": (sum(cyc_t) / max(1e-12, sum(attn_t) + sum(cyc_t))),
-        "decode_path": st.decode_path, "error_word": st.read_error(),
+        "decode_path": st.decode_path, "error_word": st.read_error(), "ledger_fold_timed": fold,
     }
     if not quiet:
         print(json.dumps(res))
@@ -206,8 +210,10 @@ def run_mha_spikes(batch=16, steps=256, warmup=8, prompt=16384, sticky=8, qwin=6
         ev[0].record()
         qr = st.append(q, kn, vn)
         ev[1].record()
-        st.attend(qr, out)
+        st.attend(qr, out, fold=fold)
         ev[2].record()
+        if not fold:
+            st.fold()
         t = (st.n_tokens - st.prompt_len - 1) % OMEGA + 1
         cyc = st.cycle_due()
         if cyc:
@@ -258,6 +264,7 @@ def main():
     ap.add_argument("--local", type=int, default=512)
     ap.add_argument("--prefill", type=int, default=0, help="time one layer's prefill lane at this prompt length")
     ap.add_argument("--mha-spikes", action="store_true", help="the batch-sharded MHA workload with planted spikes")
+    ap.add_argument("--nofold", action="store_true", help="time the attention without its vote-ledger fold")
     a = ap.parse_args()
     if a.mha_spikes:
         run_mha_spikes(batch=a.batch if a.batch != 64 else 16, steps=a.steps if a.steps != 1000 else 256,
@@ -266,7 +273,7 @@ def main():
     if a.prefill:
         run_prefill(a.prefill, steps=max(1, min(a.steps, 20)))
         return
-    run(a.batch, a.steps, a.warmup, a.sticky, a.qwin, a.local)
+    run(a.batch, a.steps, a.warmup, a.sticky, a.qwin, a.local, fold=not a.nofold)
 
 
 if __name__ == "__main__":
