@@ -210,10 +210,8 @@ def run_mha_spikes(batch=16, steps=256, warmup=8, prompt=16384, sticky=8, qwin=6
         ev[0].record()
         qr = st.append(q, kn, vn)
         ev[1].record()
-        st.attend(qr, out, fold=fold)
+        st.attend(qr, out)
         ev[2].record()
-        if not fold:
-            st.fold()
         t = (st.n_tokens - st.prompt_len - 1) % OMEGA + 1
         cyc = st.cycle_due()
         if cyc:
