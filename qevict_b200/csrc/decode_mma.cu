@@ -200,7 +200,8 @@ __device__ __forceinline__ float group_prob_sum4(uint2 u, const float* sM, const
 // weights [G][2*64], per-head totals and one liveness code per 64-token block
 // of the unit.
 constexpr int MM_CMB_MAXBLK = 1024;
-constexpr int MM_CMB_SMEM = 2 * MM_G * 128 + 2 * MM_G + MM_CMB_MAXBLK / 4;
+constexpr int MM_CMB_MAXP = 128;   // partials per (sequence, head, zone): CTAs covering one zone
+constexpr int MM_CMB_SMEM = 2 * MM_G * 2 * MM_CMB_MAXP + 2 * MM_G + MM_CMB_MAXBLK / 4;
 
 // One combine unit of one (sequence, KV head) bh: the per-CTA partials'
 // maxima and sums give the head totals; with OUT, this unit's slice of the
@@ -220,12 +221,12 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
                                              const float* __restrict__ partial, const void* __restrict__ logits,
                                              const MmPlan& P, int N0, long long bh, int chunk, int nchunks,
                                              int blocks_per_chunk, float* sm, int tid, int nthr, Sync sync) {
-    constexpr int MAXP = 64;
+    constexpr int MAXP = MM_CMB_MAXP;
     constexpr int RW = 4;   // work items per thread per round
     constexpr int XP = 16;  // partial outputs of one element loaded per round
     float(*s_m)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm);             // maxima, then weights
-    float(*s_l)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm + MM_G * 128);
-    float* s_M = sm + 2 * MM_G * 128;
+    float(*s_l)[2 * MAXP] = reinterpret_cast<float(*)[2 * MAXP]>(sm + MM_G * 2 * MAXP);
+    float* s_M = sm + 2 * MM_G * 2 * MAXP;
     float* s_L = s_M + MM_G;
     unsigned char* s_live = reinterpret_cast<unsigned char*>(s_L + MM_G);
     using T = typename Elt<DT>::T;
@@ -299,6 +300,12 @@ __device__ __forceinline__ void combine_unit(const Geo& g, const qv_layer& L, vo
     if (am >= 0) {
         s_m[am / np][am % np] = pm;
         s_l[am / np][am % np] = pl;
+    }
+    // heads spread over many CTAs (few sequences x heads): more partials than threads
+    for (int a2 = tid + nthr; a2 < G * np; a2 += nthr) {
+        const float* pr = prow(a2 % np) + (a2 / np) * 130;
+        s_m[a2 / np][a2 % np] = __ldcg(pr);
+        s_l[a2 / np][a2 % np] = __ldcg(pr + 1);
     }
     if (FOLD) {
         for (int blk = lb; blk < blk1; blk += nthr) {
@@ -1081,7 +1088,7 @@ size_t mm_ws_bytes(const Geo& g, size_t* off_part, size_t* off_logits) {
 int mm_launch(const Geo& g, const qv_layer& L, const void* q, void* out, void* ws, cudaStream_t s, int mode) {
     MmPlan P = mm_plan(g);
     // a warp group may wait on a stage only one fill ahead of it: stages >= groups
-    if (P.pmax > 64 || P.ns < P.cw / MM_SPLIT) return QV_EINVAL;
+    if (P.pmax > MM_CMB_MAXP || P.ns < P.cw / MM_SPLIT) return QV_EINVAL;
     size_t op, ol;
     mm_ws_bytes(g, &op, &ol);
     char* base = reinterpret_cast<char*>(ws);

@@ -413,6 +413,19 @@ def test_decode_c3_shape_bf16():
     assert s["cycles"] == 2 and s["fast"] and s["items_per_cta"] >= 20
 
 
+def test_decode_one_head_over_many_ctas_bf16():
+    """One sequence, one KV head (the per-GPU shape of the 131072-token
+    workload split one KV head per GPU): 64 sticky + 128 INT8 Q windows, so
+    the head's 276 items spread over every CTA and each zone's partials come
+    from more CTAs than the combine has threads per head (the merge loads them
+    in rounds).  70 steps, one cycle: plain max-abs <= 2e-3, the given-logits
+    bound, bit-exact state after the cycle."""
+    s = run_parity("bf16", B=1, H=1, G=4, D=128, sink=64, local=512, kw=64, qw=128, n_prompt_windows=208,
+                   steps=70, churn=False, q_std=1.0, kv_std=1.0, maxW=256, max_context=16384,
+                   e2e_max_abs=E2E_MAX_ABS["bf16"])
+    assert s["cycles"] == 1 and s["fast"]
+
+
 @pytest.mark.parametrize("dt", ["fp32", "bf16"])
 def test_free_running_window_sets(dt):
     """No ledger copy: GPU and oracle each fold their own probabilities into
