@@ -1,5 +1,6 @@
 """Prefill lane (qv_prefill_attention) against the oracle, at sizes that cross the
-512-query chunk boundary (GQA group 4 and MHA).
+512-query chunk boundary (GQA groups 1, 2, 4 and 8; head_dim 64 and 128;
+lengths that end inside a query block).
 
 * fp32 (CUDA-core lane): the output against the exact causal attention
   (oracle.prefill.causal_attention, float64 rounded once) within 1e-5, and the
@@ -31,7 +32,8 @@ def _cuda():
 
 
 @pytest.mark.parametrize("dt", ["fp32", "bf16", "fp16"])
-@pytest.mark.parametrize("Hq,H,D,S", [(8, 2, 128, 600), (2, 2, 64, 1100)])
+@pytest.mark.parametrize("Hq,H,D,S", [(8, 2, 128, 600), (2, 2, 64, 1100), (16, 2, 128, 700), (4, 2, 128, 517),
+                                      (8, 1, 64, 530)])
 def test_prefill_lane_vs_oracle(dt, Hq, H, D, S):
     from qevict_b200.model import prefill_attention
     g = torch.Generator().manual_seed(S + Hq)
