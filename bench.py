@@ -633,6 +633,40 @@ def run_tp(args):
     raw_ms = max_over_ranks_on(start.elapsed_time(end), world, dev)
     added_ms = (K / om - cycles) * cycle_extra_ms
     ms = raw_ms + added_ms
+    # the collectives of one plain step alone (same sizes, same group), captured
+    # in a graph and replayed: the latency floor the exchange puts under a token
+    coll_ms = None
+    if world > 1:
+        xs = torch.zeros(1, model.s.hidden, dtype=torch.bfloat16, device=dev)
+        key = torch.zeros(1, dtype=torch.int64, device=dev)
+
+        def collectives():
+            for _ in range(2 * model.s.layers):
+                dist.all_reduce(xs, op=dist.ReduceOp.SUM, group=model.group)
+            dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.group)
+
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            collectives()
+        torch.cuda.current_stream().wait_stream(side)
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            collectives()
+        for _ in range(3):
+            cg.replay()
+        dist.barrier()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_rep = 20
+        c0.record()
+        for _ in range(n_rep):
+            cg.replay()
+        c1.record()
+        torch.cuda.synchronize()
+        coll_ms = max_over_ranks_on(c0.elapsed_time(c1) / n_rep, world, dev)
+        del cg
+        dist.barrier()
     # per layer: gemv x4, rope_append, decode_mma, fold, add_rmsnorm x2, silu_mul (+ torch's
     # argmax pieces per step); per cycle and layer: count + ext
     launches = K * (10 * model.s.layers + 3) + cycles * 2 * model.s.layers
@@ -651,7 +685,9 @@ def run_tp(args):
                                           "added_ms": added_ms, "device_timed_ms": raw_ms},
                            "collectives_per_step": {"all_reduce_sum_bf16_hidden": 2 * model.s.layers,
                                                     "all_reduce_max_int64": 1,
-                                                    "all_reduce_min_int32_per_cycle": model.s.layers}},
+                                                    "all_reduce_min_int32_per_cycle": model.s.layers},
+                           "collectives_alone_ms_per_step": coll_ms,
+                           "collectives_share_of_step": None if coll_ms is None else coll_ms / (ms / K)},
                 "step_roofline": {"bound": "hbm", "bytes_per_step_per_gpu": step_bytes,
                                   "achieved": step_bytes / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                                   "frac": step_bytes / (ms / K * 1e-3) / 1e9 / peak, "peak_source": peak_kind},
