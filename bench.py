@@ -549,7 +549,7 @@ def run_ours(args):
                            + ", eviction cycles at 1 per 64 tokens"),
                 "port_vs_reference": port_vs_reference()}
         print(json.dumps(line), flush=True)
-    model.graphs.clear()
+    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -584,7 +584,7 @@ def run_tp(args):
     prompt = args.tp_prompt
     sticky = StickyShape(k_windows=64, q_windows=128)
     model = TpStickyLlamaDecoder(LlamaShape(), sticky, rank, world, batch=1, max_pos=prompt + 4096, device=dev,
-                                 seed=1234)
+                                 seed=1234, peer_sum=not args.tp_nccl)
     g = torch.Generator(device=dev)
     g.manual_seed(99)
     ids = torch.randint(0, model.s.vocab, (1, prompt), generator=g, device=dev)
@@ -635,38 +635,46 @@ def run_tp(args):
     ms = raw_ms + added_ms
     # the collectives of one plain step alone (same sizes, same group), captured
     # in a graph and replayed: the latency floor the exchange puts under a token
-    coll_ms = None
+    coll_ms = coll_nccl_ms = None
     if world > 1:
         xs = torch.zeros(1, model.s.hidden, dtype=torch.bfloat16, device=dev)
         key = torch.zeros(1, dtype=torch.int64, device=dev)
 
-        def collectives():
-            for _ in range(2 * model.s.layers):
-                dist.all_reduce(xs, op=dist.ReduceOp.SUM, group=model.group)
-            dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.group)
+        def time_collectives(nccl_only):
+            def collectives():
+                for _ in range(2 * model.s.layers):
+                    if nccl_only:
+                        dist.all_reduce(xs, op=dist.ReduceOp.SUM, group=model.group)
+                    else:
+                        model._sum(xs)
+                dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.group)
 
-        side = torch.cuda.Stream(device=dev)
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            collectives()
-        torch.cuda.current_stream().wait_stream(side)
-        cg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(cg):
-            collectives()
-        for _ in range(3):
-            cg.replay()
-        dist.barrier()
-        torch.cuda.synchronize()
-        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_rep = 20
-        c0.record()
-        for _ in range(n_rep):
-            cg.replay()
-        c1.record()
-        torch.cuda.synchronize()
-        coll_ms = max_over_ranks_on(c0.elapsed_time(c1) / n_rep, world, dev)
-        del cg
-        dist.barrier()
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                collectives()
+            torch.cuda.current_stream().wait_stream(side)
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg):
+                collectives()
+            for _ in range(3):
+                cg.replay()
+            dist.barrier()
+            torch.cuda.synchronize()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n_rep = 20
+            c0.record()
+            for _ in range(n_rep):
+                cg.replay()
+            c1.record()
+            torch.cuda.synchronize()
+            t = max_over_ranks_on(c0.elapsed_time(c1) / n_rep, world, dev)
+            del cg
+            dist.barrier()
+            return t
+
+        coll_ms = time_collectives(False)
+        coll_nccl_ms = time_collectives(True)
     # per layer: gemv x4, rope_append, decode_mma, fold, add_rmsnorm x2, silu_mul (+ torch's
     # argmax pieces per step); per cycle and layer: count + ext
     launches = K * (10 * model.s.layers + 3) + cycles * 2 * model.s.layers
@@ -687,13 +695,15 @@ def run_tp(args):
                                                     "all_reduce_max_int64": 1,
                                                     "all_reduce_min_int32_per_cycle": model.s.layers},
                            "collectives_alone_ms_per_step": coll_ms,
+                           "collectives_alone_all_nccl_ms_per_step": coll_nccl_ms,
+                           "hidden_sums": "qv_peer_sum (NVLink peer stores)" if model.ps is not None else "NCCL",
                            "collectives_share_of_step": None if coll_ms is None else coll_ms / (ms / K)},
                 "step_roofline": {"bound": "hbm", "bytes_per_step_per_gpu": step_bytes,
                                   "achieved": step_bytes / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                                   "frac": step_bytes / (ms / K * 1e-3) / 1e9 / peak, "peak_source": peak_kind},
                 "gpu_launches": launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
-    model.graphs.clear()
+    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -708,6 +718,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=8, help="tokens the host baseline times (rank 0, N=1)")
     ap.add_argument("--tp", action="store_true", help="the long-context workload, KV heads split over the ranks")
     ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
+    ap.add_argument("--tp-nccl", action="store_true", help="--tp with NCCL for the decode sums (no qv_peer_sum)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -319,6 +319,27 @@ int qv_track_positions(int32_t max_context, int32_t heads, int64_t counter, int3
 
 /* ---- diagnostics ------------------------------------------------------- */
 int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* synchronises the stream */
+/* ---- one-shot sum across the GPUs of a node (KV-head tensor parallelism) ---
+ * Not part of the reference, which runs one GPU: the all-reduce of the
+ * row-parallel decode partials ([batch, hidden] bf16 per layer) when the
+ * decoder is split by KV head over up to 8 GPUs of one node.  Each rank
+ * allocates one buffer (create), publishes its CUDA IPC handle, maps every
+ * other rank's buffer (open), then each call stores its vector into every
+ * rank's buffer over NVLink, raises a flag at each, waits (bounded) for every
+ * rank's flag and sums the vectors in rank order in fp32, rounded once to
+ * bf16: the same bits on every rank.  Every rank must make the same calls in
+ * the same order on one stream each (the call is capturable like any kernel);
+ * in and out may alias; n a multiple of 8, n*2 <= max_bytes, 16-byte aligned.
+ * A wait that gives up sets QV_DERR_TIMEOUT (qv_peer_sum_read_error). */
+#define QV_PEER_HANDLE_BYTES 64
+typedef struct qv_peer_sum qv_peer_sum;
+int qv_peer_sum_create(int32_t rank, int32_t world, size_t max_bytes, qv_peer_sum** out,
+                       void* handle /* QV_PEER_HANDLE_BYTES, to publish */);
+int qv_peer_sum_open(qv_peer_sum* ps, const void* handles /* world x QV_PEER_HANDLE_BYTES, rank order */);
+int qv_peer_sum_bf16(qv_peer_sum* ps, const void* in, void* out, int64_t n, qv_stream_t stream);
+int qv_peer_sum_read_error(qv_peer_sum* ps, int32_t* host_err, qv_stream_t stream); /* synchronises */
+int qv_peer_sum_destroy(qv_peer_sum* ps); /* after every rank's last call has completed */
+
 const char* qv_last_cuda_error(void);
 const char* qv_version(void);
 

@@ -13,6 +13,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "li
 QV_OK, QV_EINVAL, QV_ENOTALIGNED, QV_ESPACE, QV_ECUDA = 0, -1, -2, -3, -4
 QV_F32, QV_BF16, QV_F16 = 0, 1, 2
 QV_DERR_TABLE, QV_DERR_LAYOUT, QV_DERR_CAPACITY, QV_DERR_TIMEOUT = 1, 2, 4, 8
+QV_PEER_HANDLE_BYTES = 64
 QV_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024   # include/qevict_b200.h
 
 _ERRNAMES = {QV_EINVAL: "invalid argument", QV_ENOTALIGNED: "prompt/local zone not window-aligned",
@@ -86,6 +87,11 @@ def lib():
         "qv_track_decode": (ctypes.c_int, [i32, i32, i64, i64, i32, i32, vp, i32, vp, vp, vp]),
         "qv_track_positions": (ctypes.c_int, [i32, i32, i64, i32, vp, vp, i32, vp, vp, vp]),
         "qv_read_error": (ctypes.c_int, [Lp, P(i32), vp]),
+        "qv_peer_sum_create": (ctypes.c_int, [i32, i32, sz, P(vp), vp]),
+        "qv_peer_sum_open": (ctypes.c_int, [vp, ctypes.c_char_p]),
+        "qv_peer_sum_bf16": (ctypes.c_int, [vp, vp, vp, i64, vp]),
+        "qv_peer_sum_read_error": (ctypes.c_int, [vp, P(i32), vp]),
+        "qv_peer_sum_destroy": (ctypes.c_int, [vp]),
         "qv_last_cuda_error": (ctypes.c_char_p, []),
         "qv_version": (ctypes.c_char_p, []),
     }
@@ -108,6 +114,8 @@ def exported_symbols():
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_gemv",
             "qv_argmax_workspace_bytes", "qv_argmax", "qv_track_prefill", "qv_track_decode",
             "qv_track_positions", "qv_read_error",
+            "qv_peer_sum_create", "qv_peer_sum_open", "qv_peer_sum_bf16", "qv_peer_sum_read_error",
+            "qv_peer_sum_destroy",
             "qv_last_cuda_error", "qv_version"]
 
 

@@ -20,8 +20,11 @@ heads, and the matching slices of every projection:
 Per eviction cycle each layer takes one MIN all-reduce of a [B] int32 count:
 the reference's only coupling between heads (eviction_manager.py:335-345,
 the number of Q-cache losers is the minimum over heads), through
-qv_evict_cycle_count / qv_evict_cycle_ext.  Every collective is an NCCL call
-on the decode stream, captured with the kernels in the step's CUDA graph.
+qv_evict_cycle_count / qv_evict_cycle_ext.  The decode-size sums
+([B, hidden] bf16) go through qv_peer_sum (one kernel: stores into every
+rank's buffer over NVLink, a flag hand-off, a rank-order sum); the prefill's
+large sums, the greedy token's MAX and the cycle's MIN are NCCL calls.  All
+run on the decode stream, captured with the kernels in the step's CUDA graph.
 
 Weights are random (uniform-free normal, std 0.02), each matrix drawn whole
 from a generator seeded by (seed, layer, matrix) and then sliced, so the N-rank
@@ -49,7 +52,7 @@ class TpStickyLlamaDecoder:
     """This rank's share of a KV-head-parallel Llama decoder (batch B, greedy decode)."""
 
     def __init__(self, shape: LlamaShape, sticky: StickyShape, rank, world, group=None, batch=1, max_pos=40960,
-                 dtype=torch.bfloat16, device="cuda", seed=0, std=0.02):
+                 dtype=torch.bfloat16, device="cuda", seed=0, std=0.02, peer_sum=True):
         import torch.distributed as dist
         s = shape
         if s.kv_heads % world or s.ffn % world or s.vocab % world:
@@ -104,11 +107,30 @@ class TpStickyLlamaDecoder:
         self.logits = torch.empty(B, vl, dtype=dtype, device=dev)
         self.key = torch.empty(B, dtype=torch.int64, device=dev)
         self.graphs = {}
+        # the decode-size all-reduces ([B, hidden] bf16) over NVLink peer memory
+        self.ps = None
+        if peer_sum and world > 1 and dev.type == "cuda" and dtype == torch.bfloat16:
+            from .peer_sum import PeerSum
+            self.ps = PeerSum(rank, world, group, max_bytes=max(64 * 1024, -(-B * s.hidden * 2 // 16) * 16))
 
     # ------------------------------------------------------------ collectives
     def _sum(self, t):
         if self.world > 1:
-            self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
+            if self.ps is not None and self.ps.fits(t):
+                self.ps.sum_(t)
+            else:
+                self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
+
+    def close(self):
+        """Release the captured graphs and the peer-sum buffer (every rank, after
+        its last step; the ranks synchronise here)."""
+        self.graphs.clear()
+        if self.ps is not None:
+            torch.cuda.synchronize(self.device)
+            if self.world > 1:
+                self.dist.barrier(group=self.group)
+            self.ps.close()
+            self.ps = None
 
     def _greedy(self, logits):
         """Greedy token over the vocabulary shards: the local best value and index

@@ -71,7 +71,9 @@ def _rank(rank, world, port, q):
             m.step_eager()
             toks.append(int(m.tok[0]))
         ids_tp = [m.states[0].view_sticky(0)[0]]
-        m.graphs.clear()
+        if m.ps is not None:
+            assert m.ps.read_error() == 0
+        m.close()
         if rank == 0:
             one = _model(0, 1)
             one.prefill(_ids())
