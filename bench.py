@@ -549,7 +549,7 @@ def run_ours(args):
                            + ", eviction cycles at 1 per 64 tokens"),
                 "port_vs_reference": port_vs_reference()}
         print(json.dumps(line), flush=True)
-    model.close()
+    model.graphs.clear()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

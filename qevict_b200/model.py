@@ -263,6 +263,10 @@ class StickyLlamaDecoder:
         self._step_body(self.cycle_next())
         return self.next_tok
 
+    def close(self):
+        """Release the captured graphs."""
+        self.graphs.clear()
+
     @torch.no_grad()
     def capture(self):
         """Capture the plain and the cycle step into CUDA graphs (host counters restored)."""
