@@ -325,9 +325,10 @@ int qv_read_error(const qv_layer* L, int32_t* host_err, qv_stream_t stream); /* 
  * decoder is split by KV head over up to 8 GPUs of one node.  Each rank
  * allocates one buffer (create), publishes its CUDA IPC handle, maps every
  * other rank's buffer (open), then each call stores its vector into every
- * rank's buffer over NVLink, raises a flag at each, waits (bounded) for every
- * rank's flag and sums the vectors in rank order in fp32, rounded once to
- * bf16: the same bits on every rank.  Every rank must make the same calls in
+ * rank's buffer over NVLink as 8-byte words tagged with the call's epoch,
+ * waits (bounded) until every rank's words of the epoch are in its own
+ * buffer and sums the vectors in rank order in fp32, rounded once to bf16:
+ * the same bits on every rank.  Every rank must make the same calls in
  * the same order on one stream each (the call is capturable like any kernel);
  * in and out may alias; n a multiple of 8, n*2 <= max_bytes, 16-byte aligned.
  * A wait that gives up sets QV_DERR_TIMEOUT (qv_peer_sum_read_error). */
