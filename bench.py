@@ -647,7 +647,10 @@ def run_tp(args):
                         dist.all_reduce(xs, op=dist.ReduceOp.SUM, group=model.group)
                     else:
                         model._sum(xs)
-                dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.group)
+                if nccl_only or model.ps is None:
+                    dist.all_reduce(key, op=dist.ReduceOp.MAX, group=model.group)
+                else:
+                    model.ps.max_(key)
 
             side = torch.cuda.Stream(device=dev)
             side.wait_stream(torch.cuda.current_stream())
@@ -696,7 +699,8 @@ def run_tp(args):
                                                     "all_reduce_min_int32_per_cycle": model.s.layers},
                            "collectives_alone_ms_per_step": coll_ms,
                            "collectives_alone_all_nccl_ms_per_step": coll_nccl_ms,
-                           "hidden_sums": "qv_peer_sum (NVLink peer stores)" if model.ps is not None else "NCCL",
+                           "decode_collectives": ("qv_peer_sum / qv_peer_max_i64 (NVLink peer stores)"
+                                                  if model.ps is not None else "NCCL"),
                            "collectives_share_of_step": None if coll_ms is None else coll_ms / (ms / K)},
                 "step_roofline": {"bound": "hbm", "bytes_per_step_per_gpu": step_bytes,
                                   "achieved": step_bytes / (ms / K * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",

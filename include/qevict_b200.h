@@ -338,6 +338,9 @@ int qv_peer_sum_create(int32_t rank, int32_t world, size_t max_bytes, qv_peer_su
                        void* handle /* QV_PEER_HANDLE_BYTES, to publish */);
 int qv_peer_sum_open(qv_peer_sum* ps, const void* handles /* world x QV_PEER_HANDLE_BYTES, rank order */);
 int qv_peer_sum_bf16(qv_peer_sum* ps, const void* in, void* out, int64_t n, qv_stream_t stream);
+/* The same hand-off for n int64 values, their maximum over the ranks (the
+ * greedy token's packed (value, index) key); n*16 <= 2*max_bytes, 8-byte aligned. */
+int qv_peer_max_i64(qv_peer_sum* ps, const int64_t* in, int64_t* out, int64_t n, qv_stream_t stream);
 int qv_peer_sum_read_error(qv_peer_sum* ps, int32_t* host_err, qv_stream_t stream); /* synchronises */
 int qv_peer_sum_destroy(qv_peer_sum* ps); /* after every rank's last call has completed */
 

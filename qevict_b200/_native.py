@@ -90,6 +90,7 @@ def lib():
         "qv_peer_sum_create": (ctypes.c_int, [i32, i32, sz, P(vp), vp]),
         "qv_peer_sum_open": (ctypes.c_int, [vp, ctypes.c_char_p]),
         "qv_peer_sum_bf16": (ctypes.c_int, [vp, vp, vp, i64, vp]),
+        "qv_peer_max_i64": (ctypes.c_int, [vp, vp, vp, i64, vp]),
         "qv_peer_sum_read_error": (ctypes.c_int, [vp, P(i32), vp]),
         "qv_peer_sum_destroy": (ctypes.c_int, [vp]),
         "qv_last_cuda_error": (ctypes.c_char_p, []),
@@ -114,7 +115,7 @@ def exported_symbols():
             "qv_quantize_k", "qv_quantize_v", "qv_dequantize", "qv_add_rmsnorm", "qv_silu_mul", "qv_gemv",
             "qv_argmax_workspace_bytes", "qv_argmax", "qv_track_prefill", "qv_track_decode",
             "qv_track_positions", "qv_read_error",
-            "qv_peer_sum_create", "qv_peer_sum_open", "qv_peer_sum_bf16", "qv_peer_sum_read_error",
+            "qv_peer_sum_create", "qv_peer_sum_open", "qv_peer_sum_bf16", "qv_peer_max_i64", "qv_peer_sum_read_error",
             "qv_peer_sum_destroy",
             "qv_last_cuda_error", "qv_version"]
 

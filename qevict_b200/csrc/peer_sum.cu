@@ -51,12 +51,35 @@ __device__ __forceinline__ unsigned long long ps_load_word(const unsigned char* 
     return v;
 }
 
+// The data half of this rank's slot-q word at wp once it carries the epoch
+// (bounded: after about 5 s the error word is raised and later waits of the
+// call are skipped).
+__device__ __forceinline__ uint32_t ps_wait_word(const unsigned char* wp, unsigned long long tag, bool& timed_out,
+                                                 int* err) {
+    unsigned long long w = ps_load_word(wp);
+    if ((w & 0xFFFFFFFF00000000ull) != tag && !timed_out) {
+        const uint64_t t0 = global_ns();
+        while ((w & 0xFFFFFFFF00000000ull) != tag) {
+            w = ps_load_word(wp);
+            if (global_ns() - t0 > 5000000000ull) {
+                atomicOr(err, QV_DERR_TIMEOUT);
+                timed_out = true;
+                break;
+            }
+        }
+    }
+    return (uint32_t)w;
+}
+
+// MAX64 = false: nw words = bf16 pairs, summed.  MAX64 = true: nw / 2 int64
+// values (low word first), their maximum.
+template <bool MAX64>
 __global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PsArgs a, const uint32_t* __restrict__ in,
                                                               uint32_t* __restrict__ out, int nw) {
     __shared__ unsigned long long s_epoch;
     // a programmatic dependent: `in` is written by the preceding kernel; the
     // kernel after this one may be scheduled now (it waits for this grid
-    // before reading the sum)
+    // before reading the result)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) s_epoch = *a.epoch + 1;
@@ -70,31 +93,33 @@ __global__ void __launch_bounds__(PS_THREADS) peer_sum_kernel(PsArgs a, const ui
         const unsigned long long w = tag | in[i];
         for (int p = 0; p < a.world; ++p) ps_store_word(a.data[p] + slot_off + 8 * (size_t)i, w);
     }
-    // 2. every rank's words of this epoch, summed in rank order
+    // 2. every rank's words of this epoch, reduced in rank order
     const unsigned char* base = a.my_data + (size_t)par * a.world * (size_t)a.slot_bytes;
     bool timed_out = false;
-    for (int i = threadIdx.x; i < nw; i += blockDim.x) {
-        float lo = 0.f, hi = 0.f;
-        for (int q = 0; q < a.world; ++q) {
-            const unsigned char* wp = base + (size_t)q * a.slot_bytes + 8 * (size_t)i;
-            unsigned long long w = ps_load_word(wp);
-            if ((w & 0xFFFFFFFF00000000ull) != tag && !timed_out) {
-                const uint64_t t0 = global_ns();
-                while ((w & 0xFFFFFFFF00000000ull) != tag) {
-                    w = ps_load_word(wp);
-                    if (global_ns() - t0 > 5000000000ull) {
-                        atomicOr(a.err, QV_DERR_TIMEOUT);
-                        timed_out = true;
-                        break;
-                    }
-                }
+    if (!MAX64) {
+        for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+            float lo = 0.f, hi = 0.f;
+            for (int q = 0; q < a.world; ++q) {
+                const uint32_t d = ps_wait_word(base + (size_t)q * a.slot_bytes + 8 * (size_t)i, tag, timed_out, a.err);
+                lo += __uint_as_float(d << 16);
+                hi += __uint_as_float(d & 0xFFFF0000u);
             }
-            const uint32_t d = (uint32_t)w;
-            lo += __uint_as_float(d << 16);
-            hi += __uint_as_float(d & 0xFFFF0000u);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+            out[i] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-        out[i] = *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+        for (int j = threadIdx.x; j < nw / 2; j += blockDim.x) {
+            long long best = 0;
+            for (int q = 0; q < a.world; ++q) {
+                const unsigned char* wp = base + (size_t)q * a.slot_bytes + 16 * (size_t)j;
+                const uint32_t lo = ps_wait_word(wp, tag, timed_out, a.err);
+                const uint32_t hi = ps_wait_word(wp + 8, tag, timed_out, a.err);
+                const long long v = (long long)(((unsigned long long)hi << 32) | lo);
+                best = q == 0 || v > best ? v : best;
+            }
+            out[2 * j] = (uint32_t)best;
+            out[2 * j + 1] = (uint32_t)((unsigned long long)best >> 32);
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) *a.epoch = e;
@@ -165,9 +190,7 @@ extern "C" int qv_peer_sum_open(qv_peer_sum* p, const void* handles) {
     return QV_OK;
 }
 
-extern "C" int qv_peer_sum_bf16(qv_peer_sum* p, const void* in, void* out, int64_t n, qv_stream_t stream) {
-    if (!p || !p->opened || !in || !out || n <= 0 || n % 8 || (size_t)n * 4 > p->slot_bytes) return QV_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) return QV_EINVAL;
+static PsArgs ps_args(const qv_peer_sum* p) {
     PsArgs a;
     for (int r = 0; r < PS_MAXW; ++r) a.data[r] = r < p->world ? p->peer[r] : nullptr;
     a.my_data = p->base;
@@ -176,8 +199,24 @@ extern "C" int qv_peer_sum_bf16(qv_peer_sum* p, const void* in, void* out, int64
     a.rank = p->rank;
     a.world = p->world;
     a.slot_bytes = (long long)p->slot_bytes;
-    cudaError_t e = launch_pdl(peer_sum_kernel, dim3(1), dim3(PS_THREADS), 0, (cudaStream_t)stream, a,
+    return a;
+}
+
+extern "C" int qv_peer_sum_bf16(qv_peer_sum* p, const void* in, void* out, int64_t n, qv_stream_t stream) {
+    if (!p || !p->opened || !in || !out || n <= 0 || n % 8 || (size_t)n * 4 > p->slot_bytes) return QV_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) return QV_EINVAL;
+    PsArgs a = ps_args(p);
+    cudaError_t e = launch_pdl(peer_sum_kernel<false>, dim3(1), dim3(PS_THREADS), 0, (cudaStream_t)stream, a,
                                static_cast<const uint32_t*>(in), static_cast<uint32_t*>(out), (int)(n / 2));
+    return e == cudaSuccess ? QV_OK : set_cuda_error(e);
+}
+
+extern "C" int qv_peer_max_i64(qv_peer_sum* p, const int64_t* in, int64_t* out, int64_t n, qv_stream_t stream) {
+    if (!p || !p->opened || !in || !out || n <= 0 || (size_t)n * 16 > p->slot_bytes) return QV_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 7) return QV_EINVAL;
+    PsArgs a = ps_args(p);
+    cudaError_t e = launch_pdl(peer_sum_kernel<true>, dim3(1), dim3(PS_THREADS), 0, (cudaStream_t)stream, a,
+                               reinterpret_cast<const uint32_t*>(in), reinterpret_cast<uint32_t*>(out), (int)(2 * n));
     return e == cudaSuccess ? QV_OK : set_cuda_error(e);
 }
 

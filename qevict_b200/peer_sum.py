@@ -42,6 +42,13 @@ class PeerSum:
                                          torch.cuda.current_stream(t.device).cuda_stream), "qv_peer_sum_bf16")
         return t
 
+    def max_(self, t):
+        """t (int64, on this rank's GPU, at most max_bytes / 8 values) <- the
+        elementwise maximum of every rank's t."""
+        N.check(N.lib().qv_peer_max_i64(self.handle, N.ptr(t), N.ptr(t), t.numel(),
+                                        torch.cuda.current_stream(t.device).cuda_stream), "qv_peer_max_i64")
+        return t
+
     def read_error(self):
         err = ctypes.c_int32(0)
         N.check(N.lib().qv_peer_sum_read_error(self.handle, ctypes.byref(err),

@@ -21,10 +21,11 @@ Per eviction cycle each layer takes one MIN all-reduce of a [B] int32 count:
 the reference's only coupling between heads (eviction_manager.py:335-345,
 the number of Q-cache losers is the minimum over heads), through
 qv_evict_cycle_count / qv_evict_cycle_ext.  The decode-size sums
-([B, hidden] bf16) go through qv_peer_sum (one kernel: stores into every
-rank's buffer over NVLink, a flag hand-off, a rank-order sum); the prefill's
-large sums, the greedy token's MAX and the cycle's MIN are NCCL calls.  All
-run on the decode stream, captured with the kernels in the step's CUDA graph.
+([B, hidden] bf16) go through qv_peer_sum (one kernel: epoch-tagged stores
+into every rank's buffer over NVLink, a rank-order sum), and so does the
+greedy token's MAX (qv_peer_max_i64); the prefill's large sums and the
+cycle's MIN are NCCL calls.  All run on the decode stream, captured with the
+kernels in the step's CUDA graph.
 
 Weights are random (uniform-free normal, std 0.02), each matrix drawn whole
 from a generator seeded by (seed, layer, matrix) and then sliced, so the N-rank
@@ -142,7 +143,10 @@ class TpStickyLlamaDecoder:
         gidx = idx.to(torch.int64) + self.rank * self.vl
         self.key.copy_((ordered << 32) | (0xFFFFFFFF - gidx))
         if self.world > 1:
-            self.dist.all_reduce(self.key, op=self.dist.ReduceOp.MAX, group=self.group)
+            if self.ps is not None:
+                self.ps.max_(self.key)
+            else:
+                self.dist.all_reduce(self.key, op=self.dist.ReduceOp.MAX, group=self.group)
         return 0xFFFFFFFF - (self.key & 0xFFFFFFFF)
 
     # ---------------------------------------------------------------- prefill
