@@ -557,7 +557,8 @@ def run_ours(args):
 
 TP_PROMPT = 131072
 TP_WORKLOAD = ("Llama-3-8B-shaped full-model decode with KV-head tensor parallelism over the job's GPUs (q/k/v and "
-               "gate/up column-parallel, o_proj and down row-parallel with one NCCL all-reduce each, vocab-parallel "
+               "gate/up column-parallel, o_proj and down row-parallel with one all-reduce each -- in decode the "
+               "library's NVLink peer-store sum, NCCL with --tp-nccl and in prefill -- vocab-parallel "
                "LM head), bf16 random init, batch 1, 131072-token prompt (prefill lane: causal attention + per-key "
                "column sums seeding the ledger), then decode; Sticky-KV omega 64, sink 64, local 512, sticky 4096, "
                "INT8 Q-cache 8192")
