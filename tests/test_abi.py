@@ -84,3 +84,38 @@ def test_reference_default_omega_8_rejected():
     d = N.QvDims(1, 8, 4, 128, 8, 4, 32, 4, 4, 512, 4, N.QV_BF16, 0)
     assert N.lib().qv_decode_path(ctypes.byref(d)) == -1
     assert N.lib().qv_main_capacity(ctypes.byref(d)) == -1
+
+
+def _dims(B, H, G, D, dt):
+    return N.QvDims(B, H, G, D, 64, 0, 64, 0, 0, 1, 8, dt, 0)
+
+
+@pytest.mark.parametrize("B,H,G,D,S", [(1, 8, 4, 128, 32768), (2, 2, 1, 64, 1100), (1, 1, 8, 128, 517)])
+def test_prefill_workspace_holds_stats_partials_and_error_word(B, H, G, D, S):
+    """qv_prefill_workspace_bytes: the per-row statistics, for bf16/fp16 the
+    column-sum partials (a triangle of n (n + 1) / 2 rows of QB = 128 / G keys
+    per sequence and KV head, n = ceil(S / QB)), and 256 bytes for the error
+    word; fp32 (the CUDA-core lane) needs no partials."""
+    lib = N.lib()
+    al = lambda x: (x + 255) // 256 * 256
+    stats = al(B * H * G * S * 2 * 4)
+    QB = 128 // G
+    n = -(-S // QB)
+    partial = al(B * H * (QB * n * (n + 1) // 2) * 4)
+    got16 = lib.qv_prefill_workspace_bytes(ctypes.byref(_dims(B, H, G, D, N.QV_BF16)), S)
+    got32 = lib.qv_prefill_workspace_bytes(ctypes.byref(_dims(B, H, G, D, N.QV_F32)), S)
+    assert got16 == stats + partial + 256
+    assert got32 == stats + 256
+
+
+def test_peer_sum_rejects_bad_arguments_without_a_device():
+    """The argument checks of the peer sum run before any CUDA call."""
+    lib = N.lib()
+    h = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(N.QV_PEER_HANDLE_BYTES)
+    for rank, world, mb in ((0, 0, 1024), (2, 2, 1024), (0, 9, 1024), (0, 2, 0), (0, 2, 1000)):
+        assert lib.qv_peer_sum_create(rank, world, mb, ctypes.byref(h), buf) == N.QV_EINVAL
+    assert lib.qv_peer_sum_bf16(None, None, None, 8, None) == N.QV_EINVAL
+    assert lib.qv_peer_max_i64(None, None, None, 1, None) == N.QV_EINVAL
+    assert lib.qv_peer_sum_open(None, b"") == N.QV_EINVAL
+    assert lib.qv_peer_sum_destroy(None) == N.QV_EINVAL
