@@ -111,3 +111,31 @@ def test_every_read_name_is_defined(path):
     tree = ast.parse(open(os.path.join(ROOT, path)).read())
     problems = _check(tree)
     assert not problems, f"{path}: names read but never defined: {problems}"
+
+
+def _self_attributes(cls):
+    """Attributes a class defines or assigns to self anywhere in its methods."""
+    import inspect
+    import textwrap
+    names = set(dir(cls))
+    tree = ast.parse(textwrap.dedent(inspect.getsource(cls)))
+    for n in ast.walk(tree):
+        if (isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "self"
+                and isinstance(n.ctx, ast.Store)):
+            names.add(n.attr)
+    return names
+
+
+@pytest.mark.parametrize("func,cls", [("run_ours", "qevict_b200.model:StickyLlamaDecoder"),
+                                      ("run_tp", "qevict_b200.tp_model:TpStickyLlamaDecoder")])
+def test_bench_uses_only_attributes_the_decoder_has(func, cls):
+    """Every `model.<name>` bench.py's driver reads exists on the decoder class it builds."""
+    import importlib
+    mod, name = cls.split(":")
+    attrs = _self_attributes(getattr(importlib.import_module(mod), name))
+    tree = ast.parse(open(os.path.join(ROOT, "bench.py")).read())
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == func)
+    used = {(n.attr, n.lineno) for n in ast.walk(fn)
+            if isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "model"}
+    missing = sorted((a, line) for a, line in used if a not in attrs)
+    assert not missing, f"bench.py {func}: {name} has no {missing}"
